@@ -1,0 +1,342 @@
+"""Benchmark of the grouped-GEMM hot path (the README shape) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-moe]
+
+One JSON line on rank 0. A "step" is one grouped GEMM over cfg2: total_tokens=4096, E=8,
+K=4096, N=14336, bf16, tokens_per_expert uniform (512 each). The weights (940 MB) exceed the
+126 MB L2, so no flush is needed between steps. For N>1 (torchrun, one rank per GPU, NCCL)
+every rank runs its own cfg2 instance: the experts' work is independent (no data-path
+collective), scaling is weak and `value` is the whole-job TFLOP/s.
+
+Extra keys: `roofline` (the grouped-GEMM kernel vs the measured bf16 peak), `cpu_baseline`
+(the reference's per-expert loop on the host cores), `e2e` (the public API with host buffers),
+`clocks`, `gpu_launches`, and `moe_layer` (the expert-parallel Mixtral MoE layer, tokens/s).
+`--impl reference` times the reference's own algorithm (per-expert F.linear loop) on the CPU.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "groupedgemm-opt_b200"))
+
+T_TOK, E, K, N = 4096, 8, 4096, 14336
+FLOP_PER_STEP = 2.0 * T_TOK * N * K
+WORKLOAD = "cfg2 grouped GEMM E8 T4096 K4096 N14336 bf16, uniform tokens_per_expert"
+METRIC = "grouped_gemm_bf16_tflops"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def _traffic(kernel_key: str):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.txt), or None."""
+    try:
+        with open(os.path.join(HERE, "profiles", "traffic.txt")) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel_key:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        self.file.seek(0)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _barrier_sync(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(fn, steps, world):
+    """Device time of `steps` calls: events on the launching (current) stream, barrier + sync on
+    both sides, max over ranks. Returns (total_ms, per-step event times)."""
+    import torch
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    _barrier_sync(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        starts[i].record()
+        fn()
+        ends[i].record()
+    t1.record()
+    _barrier_sync(world)
+    total = _max_over_ranks(t0.elapsed_time(t1), world)
+    return total, [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def cpu_baseline_sample(threads: int):
+    """The reference's algorithm (per-expert F.linear on bf16 CPU tensors, benchmark.py:91-107)
+    on a bounded sample of cfg2: the first expert's 512 rows (1/8 of the step), timed once
+    after one warm-up call. Returns TFLOP/s."""
+    import torch
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import grouped_gemm_oracle as oracle
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    m = T_TOK // E
+    x = torch.randn(m, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(1, N, K, generator=g) * 0.02).to(torch.bfloat16)
+    tpe = torch.tensor([m])
+    oracle.sequential_gemm(x[:64], w, torch.tensor([64]), native=True)
+    t0 = time.perf_counter()
+    oracle.sequential_gemm(x, w, tpe, native=True)
+    dt = time.perf_counter() - t0
+    return 2.0 * m * N * K / dt / 1e12, dt
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU implementation of the path on this host."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _ = cpu_baseline_sample(threads)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    sample = "first expert of cfg2 (512x4096 @ 4096x14336, bf16 F.linear), 1/8 of a step"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": FLOP_PER_STEP / (value * 1e12) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "l2": "weights 940 MB > L2, no flush"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def moe_layer_bench(world, rank, steps, warmup):
+    """Expert-parallel Mixtral layer: T=16384 tokens in total (split over ranks), H=4096,
+    F=14336, E=8, top-2. Returns tokens/s of the whole job (max-over-ranks device time)."""
+    import torch
+    import torch.distributed as dist
+    from grouped_gemm_opt import fused_moe
+    T, H, F, Ex, k = 16384, 4096, 14336, 8, 2
+    el = Ex // world
+    tl = T // world
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    x = torch.randn(tl, H, device="cuda", generator=g).to(torch.bfloat16)
+    logits = torch.randn(tl, Ex, device="cuda", generator=g)
+    wgu = (torch.randn(el, 2 * F, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(el, H, F, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    grp = dist.group.WORLD if world > 1 else None
+    fn = lambda: fused_moe(x, logits, wgu, wd, k, ep_group=grp)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    total_ms, _ = _timed(fn, steps, world)
+    flops = 6.0 * T * k * H * F
+    return {"metric": "moe_layer_tokens_per_s", "value": T * steps / (total_ms / 1e3),
+            "unit": "tokens/s", "ms_per_step": total_ms / steps,
+            "tflops": flops * steps / (total_ms / 1e3) / 1e12,
+            "config": {"workload": "Mixtral MoE layer T16384 H4096 F14336 E8 top2",
+                       "parallelism": f"ep{world}", "scaling": "strong"},
+            "kernels_per_step": 5 if world == 1 else 5}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    world, rank, local = _dist_init()
+    import grouped_gemm_opt as ggo
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+
+    tpe_h = torch.full((E,), T_TOK // E, dtype=torch.int64)
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    x = torch.randn(T_TOK, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    tpe = tpe_h.cuda()
+    out = {}
+
+    def step():
+        out["y"] = ggo.grouped_gemm_opt(x, w, tpe)
+
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(local) as clk:
+        total_ms, per = _timed(step, args.steps, world)
+    clocks = clk.summary()
+    ms = total_ms / args.steps
+    value = world * FLOP_PER_STEP / (ms / 1e3) / 1e12
+    kern_ms = statistics.mean(per)  # one kernel per step: the launch's own device time
+    peaks, peak_src = _peaks()
+    achieved = FLOP_PER_STEP / (kern_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    ggo.check_device_errors(local)
+
+    # e2e through the public API with host buffers: H2D of the step's activations and counts
+    # from pinned memory, the call, D2H of the full output into pinned memory.
+    x_h = x.cpu().pin_memory()
+    tpe_hp = tpe_h.pin_memory()
+    y_h = torch.empty(T_TOK, N, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x)
+    tpe_d = torch.empty_like(tpe)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        tpe_d.copy_(tpe_hp, non_blocking=True)
+        y = ggo.grouped_gemm_opt(x_d, w, tpe_d)
+        y_h.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms, _ = _timed(e2e_step, max(3, args.steps // 2), world)
+    e2e_ms /= max(3, args.steps // 2)
+    e2e = {"value": world * FLOP_PER_STEP / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
+           "h2d_bytes_per_step": x.numel() * 2 + E * 8, "d2h_bytes_per_step": T_TOK * N * 2}
+
+    moe = None
+    if not args.no_moe:
+        del out["y"]
+        torch.cuda.empty_cache()
+        moe = moe_layer_bench(world, rank, max(3, args.steps // 4), 2)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, dt = cpu_baseline_sample(threads)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"first expert of cfg2 (512 rows, 60 GFLOP, bf16 F.linear), {dt:.1f} s"}
+
+    if rank == 0:
+        traffic = _traffic("grouped_gemm_cfg2")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": {"workload": WORKLOAD, "global_batch": world * T_TOK, "experts": E,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (weights 940 MB), no flush"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": UNIT, "frac": achieved / peak,
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "traffic": traffic},
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "moe_layer": moe,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

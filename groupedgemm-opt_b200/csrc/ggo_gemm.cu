@@ -1,0 +1,236 @@
+// Host side of the grouped GEMM: tensor-map encoding, per-device caches, tile choice and the
+// C-ABI entry points declared in include/ggo.h.
+//
+// Reference counterpart: csrc/grouped_gemm_kernel.cu:348-450 (grouped_gemm_forward) and :195-279
+// (launch_grouped_gemm). Differences by design: the token counts stay on the device (no
+// cudaStreamSynchronize), zero-token experts are skipped inside the kernel, and there is no
+// per-group argument buffer to build or copy.
+#include <mutex>
+
+#include "ggo.h"
+#include "ggo_gemm.cuh"
+#include "ggo_internal.h"
+
+namespace ggo {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_mu;
+EncodeTiledFn g_encode = nullptr;
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {0};
+bool g_attr_done[kMaxDevices][8] = {{false}};
+
+int get_encode(EncodeTiledFn* fn) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !ptr)
+      return GGO_ERR_CUDA;
+    g_encode = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  *fn = g_encode;
+  return GGO_OK;
+}
+
+// 2D K-major operand map: dims {K, rows}, box {64, 128}, 128-B swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16) {
+  EncodeTiledFn enc;
+  if (int st = get_encode(&enc)) return st;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), 128};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GGO_OK : GGO_ERR_CUDA;
+}
+
+template <int BN, int EPI, bool BF16>
+int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev, int slot,
+           cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  if (int st = make_map(&ma, a, p.rows, p.k, BF16)) return st;
+  if (int st = make_map(&mb, b, b_rows, p.k, BF16)) return st;
+  auto kern = grouped_gemm_kernel<BN, EPI, BF16>;
+  constexpr int smem = SmemLayout<BN>::kTotal;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_attr_done[dev][slot]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return GGO_ERR_CUDA;
+      g_attr_done[dev][slot] = true;
+    }
+  }
+  constexpr int out_bn = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
+  const int64_t ub = ((p.rows + kBM - 1) / kBM + p.num_segments) * n_tiles;  // tile upper bound
+  const int grid = static_cast<int>(ub < g_sm_count[dev] ? ub : g_sm_count[dev]);
+  if (grid <= 0) return GGO_OK;
+  kern<<<grid, kThreads, smem, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+}
+
+int device_setup(int* dev_out) {
+  int dev;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GGO_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_sm_count[dev] == 0) {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return GGO_ERR_CUDA;
+    if (major != 10) return GGO_ERR_NO_DEVICE;
+    g_sm_count[dev] = sms;
+  }
+  *dev_out = dev;
+  return GGO_OK;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int choose_bn(int tile_config, int64_t rows, int64_t n, int sms) {
+  switch (tile_config) {
+    case GGO_TILE_CO_128x128x64:
+    case GGO_TILE_PP_128x128x128:
+      return 128;
+    case GGO_TILE_CO_128x256x64:
+    case GGO_TILE_PP_128x256x64:
+      return 256;
+    default: {  // AUTO / CuBLAS_Seq: wide tiles unless they leave SMs idle
+      if (n <= 128) return 128;
+      const int64_t m_tiles = (rows + kBM - 1) / kBM;
+      const int64_t wide = m_tiles * ((n + 255) / 256);
+      return wide < sms ? 128 : 256;
+    }
+  }
+}
+
+int gemm_common(const void* input, const void* weights, void* output, const int64_t* counts,
+                int num_segments, int num_experts, int64_t rows, int64_t n, int64_t k, int dtype,
+                int tile_config, int sort_by_m, void* workspace, cudaStream_t stream, bool swiglu) {
+  if (!input || !weights || !output || !counts || !workspace) return GGO_ERR_INVALID_ARG;
+  if (num_segments <= 0 || num_experts <= 0 || rows < 0 || n <= 0 || k <= 0)
+    return GGO_ERR_INVALID_ARG;
+  if (tile_config < 0 || tile_config > GGO_TILE_CUBLAS_SEQ) return GGO_ERR_INVALID_ARG;
+  if (num_segments > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
+  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
+  if ((k % 8) || (n % 8)) return GGO_ERR_ALIGNMENT;
+  if (!aligned16(input) || !aligned16(weights) || !aligned16(output) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 3u))
+    return GGO_ERR_ALIGNMENT;
+  const int64_t b_rows = static_cast<int64_t>(num_experts) * (swiglu ? 2 * n : n);
+  if (rows > INT32_MAX || b_rows > INT32_MAX || k > INT32_MAX) return GGO_ERR_SHAPE;
+  if (rows == 0) return GGO_OK;
+  int dev;
+  if (int st = device_setup(&dev)) return st;
+
+  GemmParams p;
+  p.counts = counts;
+  p.num_segments = num_segments;
+  p.num_experts = num_experts;
+  p.rows = static_cast<int>(rows);
+  p.n_out = static_cast<int>(n);
+  p.n_b = static_cast<int>(swiglu ? 2 * n : n);
+  p.k = static_cast<int>(k);
+  p.sort_by_m = sort_by_m ? 1 : 0;
+  p.out = output;
+  p.ws = static_cast<GgoWorkspace*>(workspace);
+  const bool bf16 = dtype == GGO_DTYPE_BF16;
+  if (swiglu) {
+    return bf16 ? launch<256, kEpiSwiGLU, true>(input, weights, b_rows, p, dev, 4, stream)
+                : launch<256, kEpiSwiGLU, false>(input, weights, b_rows, p, dev, 5, stream);
+  }
+  const int bn = choose_bn(tile_config, rows, n, g_sm_count[dev]);
+  if (bn == 256)
+    return bf16 ? launch<256, kEpiStore, true>(input, weights, b_rows, p, dev, 0, stream)
+                : launch<256, kEpiStore, false>(input, weights, b_rows, p, dev, 1, stream);
+  return bf16 ? launch<128, kEpiStore, true>(input, weights, b_rows, p, dev, 2, stream)
+              : launch<128, kEpiStore, false>(input, weights, b_rows, p, dev, 3, stream);
+}
+
+}  // namespace
+}  // namespace ggo
+
+extern "C" {
+
+int ggo_version(void) { return 100; }
+
+const char* ggo_status_string(int status) {
+  switch (status) {
+    case GGO_OK: return "ok";
+    case GGO_ERR_INVALID_ARG: return "invalid argument";
+    case GGO_ERR_SHAPE: return "unsupported shape";
+    case GGO_ERR_DTYPE: return "unsupported dtype (expected bf16 or fp16)";
+    case GGO_ERR_ALIGNMENT: return "misaligned pointer or K/N not a multiple of 8";
+    case GGO_ERR_TOO_MANY_SEGMENTS: return "too many experts/segments (max 1024)";
+    case GGO_ERR_CUDA: return "CUDA call failed";
+    case GGO_ERR_NO_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case GGO_ERR_DEVICE_TIMEOUT: return "a device-side wait timed out";
+    case GGO_ERR_COUNT_MISMATCH: return "sum(tokens_per_expert) != total_tokens";
+    case GGO_ERR_NEGATIVE_COUNT: return "negative entry in tokens_per_expert";
+    default: return "unknown status";
+  }
+}
+
+size_t ggo_workspace_size(void) { return sizeof(ggo::GgoWorkspace); }
+
+int ggo_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,
+                     const int64_t* tokens_per_expert_dev, int num_experts, int64_t total_tokens,
+                     int64_t N, int64_t K, int dtype, int tile_config, int sort_by_m,
+                     void* workspace_dev, cudaStream_t stream) {
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_expert_dev, num_experts,
+                          num_experts, total_tokens, N, K, dtype, tile_config, sort_by_m,
+                          workspace_dev, stream, false);
+}
+
+int ggo_grouped_gemm_segments(const void* input_dev, const void* weights_dev, void* output_dev,
+                              const int64_t* tokens_per_segment_dev, int num_segments,
+                              int num_experts, int64_t total_tokens, int64_t N, int64_t K,
+                              int dtype, int tile_config, int sort_by_m, void* workspace_dev,
+                              cudaStream_t stream) {
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_segment_dev,
+                          num_segments, num_experts, total_tokens, N, K, dtype, tile_config,
+                          sort_by_m, workspace_dev, stream, false);
+}
+
+int ggo_grouped_gemm_swiglu(const void* x_dev, const void* w_gate_up_dev, void* h_dev,
+                            const int64_t* tokens_per_segment_dev, int num_segments,
+                            int num_experts, int64_t total_tokens, int64_t F, int64_t K, int dtype,
+                            int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  return ggo::gemm_common(x_dev, w_gate_up_dev, h_dev, tokens_per_segment_dev, num_segments,
+                          num_experts, total_tokens, F, K, dtype, GGO_TILE_AUTO, sort_by_m,
+                          workspace_dev, stream, true);
+}
+
+int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out) {
+  if (!workspace_dev || !status_out) return GGO_ERR_INVALID_ARG;
+  int code = 0;
+  auto* ws = static_cast<ggo::GgoWorkspace*>(workspace_dev);
+  if (cudaMemcpyAsync(&code, &ws->error, sizeof(int), cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return GGO_ERR_CUDA;
+  if (code != 0) {
+    const int zero = 0;
+    if (cudaMemcpyAsync(&ws->error, &zero, sizeof(int), cudaMemcpyHostToDevice, stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+      return GGO_ERR_CUDA;
+  }
+  *status_out = ggo::device_error_to_status(code);
+  return GGO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,444 @@
+// Persistent tcgen05 grouped GEMM for sm_100a.
+//
+//   out[r, :] = epilogue( in[r, :] @ W[expert(r)]^T ),  rows r grouped into contiguous segments.
+//
+// Replaces the CUTLASS SM90 Ptr-Array grouped GEMM of the reference
+// (csrc/grouped_gemm_sm90.cuh:87-152, launched from csrc/grouped_gemm_kernel.cu:195-279) with a
+// kernel built around B200 hardware:
+//
+//  * One flat tile pool across every segment. Each CTA computes the segment table (exclusive
+//    prefix sums of the per-segment row counts, optional heavy-first order) from the DEVICE copy of
+//    the counts, so the host never reads them (the reference copies them back and synchronises the
+//    stream, grouped_gemm_kernel.cu:374-381). Tiles are claimed by atomic work stealing.
+//  * No per-group tensor maps: all experts share K, so one 2D TMA map over in[T,K] and one over
+//    W viewed as [E*N, K] serve every segment. Rows of a tile past its segment's end are loaded
+//    (they belong to the next segment or are TMA zero-fill) and masked at the store.
+//  * Warp specialisation: warp 0 = TMA producer, warp 1 = single-thread tcgen05.mma issuer,
+//    warp 2 = TMEM allocator, warps 4..7 = epilogue (TMEM -> registers -> bf16 global stores).
+//    Two TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//  * Epilogues: plain store, or SwiGLU (silu(gate) * up) for the fused-MoE gate/up projection,
+//    where one 256-wide B tile holds 128 gate rows and the matching 128 up rows.
+//
+// No TMA multicast is used anywhere, so the same code is safe on every GPU count.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ggo_ptx.cuh"
+
+namespace ggo {
+
+constexpr int kBM = 128;          // rows per tile (tcgen05 M)
+constexpr int kBK = 64;           // K per pipeline stage: one 128-B swizzle atom of bf16
+constexpr int kUmmaK = 16;        // K per tcgen05.mma kind::f16
+constexpr int kMaxSegments = 1024;
+constexpr int kSchedDepth = 4;
+constexpr int kThreads = 256;
+constexpr int kGroupM = 16;       // m-tiles per raster group (L2 reuse of the weight tile)
+
+enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1 };
+
+// Error codes written to GgoWorkspace::error (first error wins).
+enum DevError {
+  kDevOk = 0,
+  kDevTimeoutProducer = 101,
+  kDevTimeoutMma = 102,
+  kDevTimeoutEpilogue = 103,
+  kDevCountMismatch = 110,  // sum(counts) != rows of the input
+  kDevNegativeCount = 111,
+};
+
+// 256 bytes of per-stream scratch. Must be zero before the first launch; each launch leaves the
+// two counters at zero again (the last CTA to finish resets them). `error` is sticky.
+struct GgoWorkspace {
+  int tile_counter;
+  int done_counter;
+  int error;
+  int pad[61];
+};
+
+struct GemmParams {
+  const int64_t* counts;  // [num_segments] rows per segment, device memory
+  int num_segments;       // <= kMaxSegments
+  int num_experts;        // segment s multiplies by expert (s % num_experts)
+  int rows;               // T = rows of `in` (and of `out`)
+  int n_out;              // columns of `out` (N, or F for SwiGLU)
+  int n_b;                // rows of one expert's W (N, or 2F for SwiGLU)
+  int k;                  // K
+  int sort_by_m;          // process segments heaviest-first
+  void* out;              // [rows, n_out], bf16 or fp16
+  GgoWorkspace* ws;
+};
+
+struct TileInfo {
+  int row0;    // first input row of the tile
+  int rows;    // valid rows (<= kBM); 0 = no more work
+  int n0;      // first output column
+  int brow0;   // first W row of box 0 (and box 1 = brow1)
+  int brow1;
+  int pad[3];
+};
+
+template <int BN>
+struct SmemLayout {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;   // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;    // 32 KB or 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTileBytes = kStages * kStageBytes;
+  static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
+  static constexpr int kMiscBytes = 1024;
+  static constexpr int kTotal = 1024 /*align slack*/ + kTileBytes + kTableBytes + kMiscBytes;
+};
+
+template <int BN, int EPI, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using L = SmemLayout<BN>;
+  constexpr int S = L::kStages;
+  constexpr int kTmemCols = 2 * BN;             // two accumulators
+  constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
+  int* t_rowoff = t_cnt + kMaxSegments;
+  int* t_order = t_rowoff + kMaxSegments;
+  int* t_tileoff = t_order + kMaxSegments;  // kMaxSegments + 1 entries
+  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* accf_bar = empty_bar + S;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* schf_bar = acce_bar + 2;
+  uint64_t* sche_bar = schf_bar + kSchedDepth;
+  TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = &p.ws->error;
+
+  // ------------------------------------------------------------------ set-up
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf_bar[i], 1);
+      mbar_init(&acce_bar[i], 4);
+    }
+    for (int i = 0; i < kSchedDepth; ++i) {
+      mbar_init(&schf_bar[i], 1);
+      mbar_init(&sche_bar[i], 1 + 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+
+  // Segment table, computed redundantly by every CTA from the device counts.
+  const int nseg = p.num_segments;
+  for (int s = threadIdx.x; s < nseg; s += kThreads) {
+    long long c = p.counts[s];
+    if (c < 0) {
+      atomicCAS(err, 0, kDevNegativeCount);
+      c = 0;
+    }
+    t_cnt[s] = c > p.rows ? p.rows : static_cast<int>(c);
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive prefix sum of rows, in segment order
+    int carry = 0;
+    for (int base = 0; base < nseg; base += 32) {
+      const int s = base + lane;
+      const int v = s < nseg ? t_cnt[s] : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (s < nseg) t_rowoff[s] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0 && carry != p.rows && blockIdx.x == 0) atomicCAS(err, 0, kDevCountMismatch);
+  }
+  // Processing order: identity, or heaviest segment first (ties by index) via a bitonic sort of
+  // 64-bit keys held temporarily in the (still unused) operand tile buffers.
+  if (p.sort_by_m && nseg > 1) {
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(tiles);
+    int n2 = 1;
+    while (n2 < nseg) n2 <<= 1;
+    for (int i = threadIdx.x; i < n2; i += kThreads) {
+      keys[i] = i < nseg ? (static_cast<unsigned long long>(0x7fffffff - t_cnt[i]) << 32) |
+                               static_cast<unsigned>(i)
+                         : ~0ull;
+    }
+    __syncthreads();
+    for (int size = 2; size <= n2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = threadIdx.x; i < n2; i += kThreads) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool up = (i & size) == 0;
+            const unsigned long long a = keys[i], b = keys[j];
+            if ((a > b) == up) {
+              keys[i] = b;
+              keys[j] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = threadIdx.x; i < nseg; i += kThreads)
+      t_order[i] = static_cast<int>(keys[i] & 0xffffffffu);
+  } else {
+    for (int i = threadIdx.x; i < nseg; i += kThreads) t_order[i] = i;
+  }
+  __syncthreads();
+  const int n_tiles = (p.n_out + kOutBN - 1) / kOutBN;
+  if (warp == 0) {  // exclusive prefix sum of tiles, in processing order
+    int carry = 0;
+    for (int base = 0; base < nseg; base += 32) {
+      const int i = base + lane;
+      const int v = i < nseg ? ((t_cnt[t_order[i]] + kBM - 1) / kBM) * n_tiles : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (i < nseg) t_tileoff[i] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) {
+      t_tileoff[nseg] = carry;
+      *total_tiles_s = carry;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = *total_tiles_s;
+  const int num_kb = (p.k + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int stage = 0, phase = 0, q = 0, qphase = 0;
+      while (true) {
+        const int t = atomicAdd(&p.ws->tile_counter, 1);
+        TileInfo info;
+        info.rows = 0;
+        if (t < total_tiles) {
+          int lo = 0, hi = nseg - 1;  // last position whose tile offset is <= t
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (t_tileoff[mid] <= t) lo = mid; else hi = mid - 1;
+          }
+          const int seg = t_order[lo];
+          const int local = t - t_tileoff[lo];
+          const int mt = (t_cnt[seg] + kBM - 1) / kBM;
+          const int group = local / (kGroupM * n_tiles);
+          const int first_m = group * kGroupM;
+          const int gm = min(kGroupM, mt - first_m);
+          const int r = local - group * kGroupM * n_tiles;
+          const int m_idx = first_m + r % gm;
+          const int n_idx = r / gm;
+          const int expert = seg % p.num_experts;
+          info.row0 = t_rowoff[seg] + m_idx * kBM;
+          info.rows = min(kBM, t_cnt[seg] - m_idx * kBM);
+          info.n0 = n_idx * kOutBN;
+          if (EPI == kEpiSwiGLU) {
+            info.brow0 = expert * p.n_b + info.n0;              // gate rows
+            info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
+          } else {
+            info.brow0 = expert * p.n_b + info.n0;
+            info.brow1 = info.brow0 + 128;
+          }
+        }
+        if (!mbar_wait(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
+        ring[q] = info;
+        mbar_arrive(&schf_bar[q]);
+        if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+        if (info.rows == 0) break;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = tiles + stage * L::kStageBytes;
+          uint8_t* b_dst = a_dst + L::kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
+          tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, info.row0);
+          tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
+          if (BN == 256) tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kBM, BN, BF16);
+      int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
+      const uint32_t tiles_addr = smem_u32(tiles);
+      while (true) {
+        if (!mbar_wait(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutMma)) break;
+        const bool valid = ring[q].rows > 0;
+        mbar_arrive(&sche_bar[q]);
+        if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+        if (!valid) break;
+        if (!mbar_wait(&acce_bar[acc], aphase ^ 1, abort_flag, err, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = tiles_addr + stage * L::kStageBytes;
+          const uint64_t adesc = sdesc_sw128_kmajor(a_addr);
+          const uint64_t bdesc = sdesc_sw128_kmajor(a_addr + L::kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            // advance 16 elements (32 B) along K inside the 128-B swizzle atom
+            mma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&accf_bar[acc]);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- epilogue
+    const int ew = warp - 4;  // TMEM lane quarter this warp may access
+    int q = 0, qphase = 0, acc = 0, aphase = 0;
+    while (true) {
+      if (!mbar_wait(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      const TileInfo info = ring[q];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sche_bar[q]);
+      if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+      if (info.rows == 0) break;
+      if (!mbar_wait(&accf_bar[acc], aphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int r_local = ew * 32 + lane;
+      const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
+      using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      OutT* out_row = reinterpret_cast<OutT*>(p.out) +
+                      static_cast<size_t>(info.row0 + r_local) * p.n_out;
+      if (EPI == kEpiStore) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + c, v);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = info.n0 + c + 8 * j;
+              if (col < p.n_out) {
+                uint4 pk;
+                uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float a = __uint_as_float(v[8 * j + 2 * h]);
+                  const float b = __uint_as_float(v[8 * j + 2 * h + 1]);
+                  if (BF16) {
+                    __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
+                  } else {
+                    __half2 t2 = __floats2half2_rn(a, b);
+                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
+                  }
+                }
+                *reinterpret_cast<uint4*>(out_row + col) = pk;
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = info.n0 + c + 8 * j;
+              if (col < p.n_out) {
+                uint4 pk;
+                uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  float y[2];
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const float gv = __uint_as_float(g[8 * j + 2 * h + e]);
+                    const float uv = __uint_as_float(u[8 * j + 2 * h + e]);
+                    y[e] = gv / (1.0f + __expf(-gv)) * uv;
+                  }
+                  if (BF16) {
+                    __nv_bfloat162 t2 = __floats2bfloat162_rn(y[0], y[1]);
+                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
+                  } else {
+                    __half2 t2 = __floats2half2_rn(y[0], y[1]);
+                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
+                  }
+                }
+                *reinterpret_cast<uint4*>(out_row + col) = pk;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+      if (++acc == 2) { acc = 0; aphase ^= 1; }
+    }
+  }
+
+  // ------------------------------------------------------------------ tear-down
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&p.ws->done_counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(&p.ws->tile_counter, 0);
+      atomicExch(&p.ws->done_counter, 0);
+    }
+  }
+}
+
+}  // namespace ggo

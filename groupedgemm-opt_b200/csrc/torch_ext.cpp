@@ -1,0 +1,213 @@
+// grouped_gemm_opt._C: thin PyTorch binding over the C ABI of libggo_b200.so (include/ggo.h).
+//
+// Replaces the reference binding csrc/torch_ext.cpp:1-27 and the torch-facing half of
+// csrc/grouped_gemm_kernel.cu:348-450. This file only validates tensors, allocates outputs and
+// per-stream workspaces through the torch caching allocator, and maps status codes to
+// RuntimeError. All arithmetic happens in the CUDA kernels behind the C ABI.
+#include <torch/extension.h>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "ggo.h"
+
+namespace {
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == GGO_OK, what, " failed: ", ggo_status_string(st), " (status ", st, ")");
+}
+
+int dtype_code(const torch::Tensor& t) {
+  if (t.scalar_type() == torch::kBFloat16) return GGO_DTYPE_BF16;
+  if (t.scalar_type() == torch::kHalf) return GGO_DTYPE_FP16;
+  TORCH_CHECK(false, "Unsupported dtype: ", t.scalar_type());
+  return -1;
+}
+
+// One zero-initialised workspace per (device, stream); kept for the life of the process.
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, torch::Tensor> g_ws;
+
+void* workspace_for(const torch::Device& dev, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  auto key = std::make_pair(static_cast<int>(dev.index()), stream);
+  auto it = g_ws.find(key);
+  if (it == g_ws.end()) {
+    auto t = torch::zeros({static_cast<int64_t>(ggo_workspace_size())},
+                          torch::TensorOptions().dtype(torch::kUInt8).device(dev));
+    it = g_ws.emplace(key, t).first;
+  }
+  return it->second.data_ptr();
+}
+
+torch::Tensor counts_on_device(const torch::Tensor& counts, const torch::Device& dev) {
+  auto c = counts.to(torch::kInt64);
+  if (!c.is_cuda() || c.device() != dev) c = c.to(dev, /*non_blocking=*/true);
+  return c.contiguous();
+}
+
+void check_operands(const torch::Tensor& input, const torch::Tensor& weights) {
+  TORCH_CHECK(input.is_cuda(), "input must be on CUDA");
+  TORCH_CHECK(weights.is_cuda(), "weights must be on CUDA");
+  TORCH_CHECK(input.dim() == 2, "input must be 2D [total_tokens, K]");
+  TORCH_CHECK(weights.dim() == 3, "weights must be 3D [num_experts, N, K]");
+  TORCH_CHECK(input.size(1) == weights.size(2), "K mismatch: input=", input.size(1),
+              " vs weights=", weights.size(2));
+  TORCH_CHECK(input.is_contiguous() && weights.is_contiguous(),
+              "input and weights must be contiguous");
+  TORCH_CHECK(input.scalar_type() == weights.scalar_type(), "input/weights dtype mismatch");
+  TORCH_CHECK(input.device() == weights.device(), "input/weights on different devices");
+}
+
+// grouped_gemm_opt_forward(input, weights, tokens_per_expert, tile_config=4, sort_by_m=True)
+// (reference csrc/torch_ext.cpp:19-27). Counts may be on the CPU or the GPU; on the GPU nothing
+// synchronises.
+torch::Tensor grouped_gemm_segments(const torch::Tensor& input, const torch::Tensor& weights,
+                                    const torch::Tensor& counts, int64_t num_experts,
+                                    int64_t tile_config, bool sort_by_m) {
+  check_operands(input, weights);
+  TORCH_CHECK(counts.dim() == 1, "tokens_per_expert must be 1D");
+  c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = input.size(0), K = input.size(1), N = weights.size(1);
+  auto out = torch::empty({T, N}, input.options());
+  if (T == 0) return out;
+  auto c = counts_on_device(counts, input.device());
+  const int st = ggo_grouped_gemm_segments(
+      input.data_ptr(), weights.data_ptr(), out.data_ptr(), c.data_ptr<int64_t>(),
+      static_cast<int>(c.size(0)), static_cast<int>(num_experts), T, N, K, dtype_code(input),
+      static_cast<int>(tile_config), sort_by_m ? 1 : 0, workspace_for(input.device(), stream),
+      stream);
+  check_status(st, "grouped GEMM");
+  return out;
+}
+
+torch::Tensor grouped_gemm_forward(const torch::Tensor& input, const torch::Tensor& weights,
+                                   const torch::Tensor& tokens_per_expert, int64_t tile_config,
+                                   bool sort_by_m) {
+  check_operands(input, weights);
+  TORCH_CHECK(tokens_per_expert.dim() == 1 && tokens_per_expert.size(0) == weights.size(0),
+              "tokens_per_expert must be 1D with num_experts entries");
+  return grouped_gemm_segments(input, weights, tokens_per_expert, weights.size(0), tile_config,
+                               sort_by_m);
+}
+
+torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
+                                  const torch::Tensor& counts, int64_t num_experts,
+                                  bool sort_by_m) {
+  check_operands(x, w_gate_up);
+  TORCH_CHECK(w_gate_up.size(1) % 2 == 0, "w_gate_up must have 2F rows per expert");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x.size(0), K = x.size(1), F = w_gate_up.size(1) / 2;
+  auto h = torch::empty({T, F}, x.options());
+  if (T == 0) return h;
+  auto c = counts_on_device(counts, x.device());
+  const int st = ggo_grouped_gemm_swiglu(
+      x.data_ptr(), w_gate_up.data_ptr(), h.data_ptr(), c.data_ptr<int64_t>(),
+      static_cast<int>(c.size(0)), static_cast<int>(num_experts), T, F, K, dtype_code(x),
+      sort_by_m ? 1 : 0, workspace_for(x.device(), stream), stream);
+  check_status(st, "gate/up SwiGLU grouped GEMM");
+  return h;
+}
+
+// Router: returns (topk_ids int32 [T,k], topk_weights fp32 [T,k], tokens_per_expert int64 [E],
+// scratch int32) -- scratch carries the per-block offsets to moe_permute.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor> moe_route(
+    const torch::Tensor& logits, int64_t top_k) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2, "router_logits must be a 2D CUDA tensor");
+  c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  auto lg = logits.to(torch::kFloat32).contiguous();
+  const int64_t T = lg.size(0), E = lg.size(1);
+  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(lg.device());
+  auto ids = torch::empty({T, top_k}, i32);
+  auto w = torch::empty({T, top_k}, lg.options());
+  auto tpe = torch::empty({E}, torch::TensorOptions().dtype(torch::kInt64).device(lg.device()));
+  const int64_t sb = static_cast<int64_t>(ggo_moe_route_scratch_bytes(T, static_cast<int>(E)));
+  auto scratch = torch::empty({(sb + 3) / 4}, i32);
+  const int st = ggo_moe_route(lg.data_ptr<float>(), T, static_cast<int>(E),
+                               static_cast<int>(top_k), ids.data_ptr<int32_t>(),
+                               w.data_ptr<float>(), tpe.data_ptr<int64_t>(), scratch.data_ptr(),
+                               stream);
+  check_status(st, "MoE router");
+  return {ids, w, tpe, scratch};
+}
+
+// Permute: returns (x_sorted [T*k,H], sorted_token int32 [T*k], slot_pos int32 [T*k]).
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> moe_permute(
+    const torch::Tensor& x, const torch::Tensor& topk_ids, const torch::Tensor& scratch,
+    int64_t num_experts) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "hidden must be 2D contiguous CUDA");
+  TORCH_CHECK(topk_ids.scalar_type() == torch::kInt32 && topk_ids.is_contiguous(),
+              "topk_ids must be contiguous int32");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x.size(0), H = x.size(1), k = topk_ids.size(1);
+  auto xs = torch::empty({T * k, H}, x.options());
+  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(x.device());
+  auto stok = torch::empty({T * k}, i32);
+  auto spos = torch::empty({T * k}, i32);
+  const int st = ggo_moe_permute(x.data_ptr(), T, H, static_cast<int>(num_experts),
+                                 static_cast<int>(k), topk_ids.data_ptr<int32_t>(), xs.data_ptr(),
+                                 stok.data_ptr<int32_t>(), spos.data_ptr<int32_t>(),
+                                 scratch.data_ptr(), dtype_code(x), stream);
+  check_status(st, "MoE permute");
+  return {xs, stok, spos};
+}
+
+torch::Tensor moe_combine(const torch::Tensor& y_sorted, const torch::Tensor& topk_weights,
+                          const torch::Tensor& slot_pos) {
+  TORCH_CHECK(y_sorted.is_cuda() && y_sorted.dim() == 2 && y_sorted.is_contiguous(),
+              "y_sorted must be 2D contiguous CUDA");
+  TORCH_CHECK(topk_weights.scalar_type() == torch::kFloat32 && topk_weights.is_contiguous(),
+              "topk_weights must be contiguous fp32");
+  TORCH_CHECK(slot_pos.scalar_type() == torch::kInt32 && slot_pos.is_contiguous(),
+              "slot_pos must be contiguous int32");
+  c10::cuda::CUDAGuard guard(y_sorted.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = topk_weights.size(0), k = topk_weights.size(1), H = y_sorted.size(1);
+  auto out = torch::empty({T, H}, y_sorted.options());
+  const int st = ggo_moe_combine(y_sorted.data_ptr(), topk_weights.data_ptr<float>(),
+                                 slot_pos.data_ptr<int32_t>(), T, H, static_cast<int>(k),
+                                 out.data_ptr(), dtype_code(y_sorted), stream);
+  check_status(st, "MoE combine");
+  return out;
+}
+
+// Reads and clears the device-side error word of the current stream's workspace (synchronises).
+int64_t workspace_error(int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int code = 0;
+  const int st = ggo_workspace_error(
+      workspace_for(torch::Device(torch::kCUDA, static_cast<c10::DeviceIndex>(device)), stream),
+      stream, &code);
+  check_status(st, "workspace error read");
+  return code;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("grouped_gemm_opt_forward", &grouped_gemm_forward,
+        "Persistent tcgen05 grouped GEMM for MoE (sm_100a)", py::arg("input"),
+        py::arg("weights"), py::arg("tokens_per_expert"), py::arg("tile_config") = 4,
+        py::arg("sort_by_m") = true);
+  m.def("grouped_gemm_segments", &grouped_gemm_segments, py::arg("input"), py::arg("weights"),
+        py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("tile_config") = 4,
+        py::arg("sort_by_m") = true);
+  m.def("grouped_gemm_swiglu", &grouped_gemm_swiglu, py::arg("x"), py::arg("w_gate_up"),
+        py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("sort_by_m") = true);
+  m.def("moe_route", &moe_route, py::arg("router_logits"), py::arg("top_k"));
+  m.def("moe_permute", &moe_permute, py::arg("hidden"), py::arg("topk_ids"), py::arg("scratch"),
+        py::arg("num_experts"));
+  m.def("moe_combine", &moe_combine, py::arg("y_sorted"), py::arg("topk_weights"),
+        py::arg("slot_pos"));
+  m.def("workspace_error", &workspace_error, py::arg("device") = 0);
+  m.def("abi_version", []() { return ggo_version(); });
+}

@@ -1,0 +1,79 @@
+"""Python API of the grouped GEMM, a drop-in for the reference's grouped_gemm_opt/ops.py.
+
+Same names, argument meaning, defaults and error behaviour as the reference
+(grouped_gemm_opt/ops.py:8-84); the work runs in the persistent tcgen05 kernel of
+libggo_b200.so through the ``_C`` binding.
+"""
+from enum import IntEnum
+
+import torch
+
+from grouped_gemm_opt._native import _C
+
+
+class TileConfig(IntEnum):
+    """Tile configuration, value-compatible with the reference enum (ops.py:8-29).
+
+    On B200 the kernel is always the persistent tcgen05 grouped GEMM; the value picks its tile:
+      Co_128x128x64 / PP_128x128x128 -- 128x128 output tile, 6-stage TMA ring
+      Co_128x256x64 / PP_128x256x64  -- 128x256 output tile, 4-stage TMA ring
+      AUTO        -- 128x256 unless that leaves SMs idle (or N <= 128), then 128x128
+      CuBLAS_Seq  -- accepted for compatibility; runs the AUTO choice (no library GEMM)
+    """
+    Co_128x128x64 = 0
+    Co_128x256x64 = 1
+    PP_128x128x128 = 2
+    PP_128x256x64 = 3
+    AUTO = 4
+    CuBLAS_Seq = 5
+
+
+def grouped_gemm_opt(
+    input: torch.Tensor,
+    weights: torch.Tensor,
+    tokens_per_expert: torch.Tensor,
+    tile_config: TileConfig = TileConfig.AUTO,
+    sort_by_m: bool = True,
+) -> torch.Tensor:
+    """MoE grouped GEMM: ``output[i] = input[i] @ weights[expert_of(i)].T``.
+
+    Args:
+        input: [total_tokens, K] bf16/fp16, rows sorted by expert.
+        weights: [num_experts, N, K] (torch.nn.Linear layout per expert).
+        tokens_per_expert: [num_experts] integer tensor on the CPU or the GPU. GPU counts are
+            read only by the kernel: the call never synchronises the host.
+        tile_config: a TileConfig (AUTO recommended).
+        sort_by_m: process experts heaviest-first (a tile-order hint; results are identical).
+
+    Returns:
+        output: [total_tokens, N], same dtype as ``input``.
+
+    Raises AssertionError for non-CUDA operands, wrong ranks and (CPU counts only)
+    ``sum(tokens_per_expert) != total_tokens`` -- as the reference (ops.py:57-64) -- and
+    RuntimeError for dtype/shape/alignment errors (as the reference's TORCH_CHECKs).
+    """
+    assert input.is_cuda and weights.is_cuda
+    assert input.dim() == 2 and weights.dim() == 3
+
+    tokens_per_expert = tokens_per_expert.to(torch.int64).contiguous()
+    if not tokens_per_expert.is_cuda:
+        total = int(tokens_per_expert.sum().item())
+        assert total == input.size(0), (
+            f"sum(tokens_per_expert)={total} != total_tokens={input.size(0)}")
+        # Zero-token experts need no host-side filtering (and no weight copy): the kernel skips
+        # them while it builds its tile pool.
+    return _C.grouped_gemm_opt_forward(
+        input.contiguous(),
+        weights.contiguous(),
+        tokens_per_expert,
+        int(tile_config),
+        sort_by_m,
+    )
+
+
+def check_device_errors(device: int = 0) -> None:
+    """Synchronises and raises RuntimeError if a kernel on the current stream recorded an error
+    (count mismatch with GPU counts, negative count, or an expired bounded wait)."""
+    code = int(_C.workspace_error(device))
+    if code:
+        raise RuntimeError(f"grouped_gemm_opt device error code {code}")

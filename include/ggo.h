@@ -1,0 +1,151 @@
+/*
+ * ggo.h - C ABI of the B200-native (sm_100a) MoE grouped-GEMM library.
+ *
+ * Plain pointers, sizes and a cudaStream_t; no PyTorch types. Every pointer argument named
+ * *_dev is device memory. Every call is stream-ordered on `stream` and never synchronises the
+ * host unless its comment says so. Return value: GGO_OK (0) or one of the GGO_ERR_* codes;
+ * ggo_status_string() turns a code into a message.
+ *
+ * Reference interfaces these entry points replace (paths inside jeshxxx/GroupedGEMM-OPT):
+ *   csrc/grouped_gemm.h:21-26          grouped_gemm::grouped_gemm_forward
+ *   csrc/grouped_gemm_kernel.cu:348-450 host dispatch (count copy, zero filter, tile choice)
+ *   csrc/grouped_gemm_kernel.cu:195-279 launch_grouped_gemm<Kernel> (CUTLASS device adapter)
+ *   csrc/torch_ext.cpp:19-27           pybind grouped_gemm_opt_forward
+ *   grouped_gemm_opt/triton_fused_moe.py:104-150  the fused-MoE entry point
+ */
+#ifndef GGO_H_
+#define GGO_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- status codes */
+#define GGO_OK 0
+#define GGO_ERR_INVALID_ARG 1     /* null pointer, negative size, bad enum value          */
+#define GGO_ERR_SHAPE 2           /* K mismatch / dimension out of the supported range     */
+#define GGO_ERR_DTYPE 3           /* dtype other than GGO_DTYPE_BF16 / GGO_DTYPE_FP16      */
+#define GGO_ERR_ALIGNMENT 4       /* pointer not 16-B aligned, K or N not a multiple of 8  */
+#define GGO_ERR_TOO_MANY_SEGMENTS 5 /* num_segments > GGO_MAX_SEGMENTS                     */
+#define GGO_ERR_CUDA 6            /* a CUDA runtime/driver call failed                     */
+#define GGO_ERR_NO_DEVICE 7       /* device is not sm_100 (B200 class)                     */
+#define GGO_ERR_DEVICE_TIMEOUT 8  /* a kernel's bounded wait expired (read back by ggo_workspace_error) */
+#define GGO_ERR_COUNT_MISMATCH 9  /* sum(tokens_per_expert) != total_tokens (detected on device) */
+#define GGO_ERR_NEGATIVE_COUNT 10 /* a token count was negative (detected on device)       */
+
+#define GGO_DTYPE_BF16 0
+#define GGO_DTYPE_FP16 1
+
+#define GGO_MAX_SEGMENTS 1024
+#define GGO_WORKSPACE_BYTES 256
+
+/* TileConfig values, identical to the reference enum (csrc/grouped_gemm.h:8-19,
+ * grouped_gemm_opt/ops.py:23-28). On sm_100a they select:
+ *   0 Co_128x128x64  -> 128x128 tcgen05 tile, 6-stage TMA ring
+ *   1 Co_128x256x64  -> 128x256 tcgen05 tile, 4-stage TMA ring
+ *   2 PP_128x128x128 -> 128x128 tile (as 0)
+ *   3 PP_128x256x64  -> 128x256 tile (as 1)
+ *   4 AUTO           -> device-free heuristic on N
+ *   5 CuBLAS_Seq     -> accepted for API compatibility; runs the AUTO choice (no library GEMM) */
+#define GGO_TILE_CO_128x128x64 0
+#define GGO_TILE_CO_128x256x64 1
+#define GGO_TILE_PP_128x128x128 2
+#define GGO_TILE_PP_128x256x64 3
+#define GGO_TILE_AUTO 4
+#define GGO_TILE_CUBLAS_SEQ 5
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int ggo_version(void);
+
+/* Human-readable message for a status code (static storage, never NULL). */
+const char* ggo_status_string(int status);
+
+/* Bytes of scratch one in-flight call needs (GGO_WORKSPACE_BYTES). The caller allocates it in
+ * device memory, zero-fills it ONCE, and reuses it for every later call on the same stream; calls
+ * that may run concurrently (different streams) need distinct workspaces. */
+size_t ggo_workspace_size(void);
+
+/* Grouped GEMM, the replacement of grouped_gemm::grouped_gemm_forward
+ * (reference csrc/grouped_gemm.h:21-26, csrc/grouped_gemm_kernel.cu:348-450):
+ *
+ *   output[r, :] = input[r, :] @ weights[e(r)]^T
+ *
+ * input_dev   [total_tokens, K]   row-major, rows sorted by expert
+ * weights_dev [num_experts, N, K] row-major (torch.nn.Linear layout per expert)
+ * output_dev  [total_tokens, N]   written for every row that belongs to an expert
+ * tokens_per_expert_dev [num_experts] int64, DEVICE memory: read only by the kernel, so the host
+ *             never waits for it (the reference copies it to the host and synchronises).
+ * Experts with zero tokens are skipped on the device with no weight copy. sum(tokens) must equal
+ * total_tokens; a mismatch is recorded in the workspace (GGO_ERR_COUNT_MISMATCH via
+ * ggo_workspace_error) and rows outside [0, total_tokens) are never read or written.
+ * K and N must be multiples of 8; pointers 16-byte aligned. */
+int ggo_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,
+                     const int64_t* tokens_per_expert_dev, int num_experts, int64_t total_tokens,
+                     int64_t N, int64_t K, int dtype, int tile_config, int sort_by_m,
+                     void* workspace_dev, cudaStream_t stream);
+
+/* Generalised form used by expert parallelism: `num_segments` contiguous row segments, segment s
+ * multiplied by expert (s % num_experts). With num_segments == num_experts it equals
+ * ggo_grouped_gemm. After an all-to-all the received rows are [source rank][local expert], i.e.
+ * exactly this layout with num_segments = world_size * local_experts. No reference counterpart
+ * (the reference is single-device). */
+int ggo_grouped_gemm_segments(const void* input_dev, const void* weights_dev, void* output_dev,
+                              const int64_t* tokens_per_segment_dev, int num_segments,
+                              int num_experts, int64_t total_tokens, int64_t N, int64_t K,
+                              int dtype, int tile_config, int sort_by_m, void* workspace_dev,
+                              cudaStream_t stream);
+
+/* Fused-MoE stage 2: gate/up grouped GEMM with the SwiGLU epilogue.
+ *   h[r, f] = silu(x[r,:] . Wgu[e, f, :]) * (x[r,:] . Wgu[e, F + f, :])
+ * w_gate_up_dev [num_experts, 2F, K]: rows 0..F-1 gate, rows F..2F-1 up.
+ * h_dev [total_tokens, F]. Segment semantics as ggo_grouped_gemm_segments. F multiple of 8.
+ * Replaces the GEMM of grouped_gemm_opt/triton_fused_moe.py:16-78 plus the activation that the
+ * reference leaves to the caller. */
+int ggo_grouped_gemm_swiglu(const void* x_dev, const void* w_gate_up_dev, void* h_dev,
+                            const int64_t* tokens_per_segment_dev, int num_segments,
+                            int num_experts, int64_t total_tokens, int64_t F, int64_t K, int dtype,
+                            int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
+/* Fused-MoE stage 1a: router. For every token t: the top_k largest logits (ties -> lower expert
+ * index), softmax over those k values (fp32), written as topk_ids [T, top_k] int32 and
+ * topk_weights [T, top_k] fp32, in descending-logit order. Also writes tokens_per_expert [E]
+ * int64. logits fp32 [T, E]. E <= 1024, top_k <= 16, top_k <= E.
+ * block_counts_dev needs ggo_moe_route_scratch_bytes(T, E) bytes. No reference counterpart. */
+size_t ggo_moe_route_scratch_bytes(int64_t num_tokens, int num_experts);
+int ggo_moe_route(const float* logits_dev, int64_t num_tokens, int num_experts, int top_k,
+                  int32_t* topk_ids_dev, float* topk_weights_dev,
+                  int64_t* tokens_per_expert_dev, void* scratch_dev, cudaStream_t stream);
+
+/* Fused-MoE stage 1b: permute. Sorted order is expert-major, then token index (each token's k
+ * experts are distinct, so the k-slot never ties). Writes
+ *   x_sorted [T*top_k, H]  the gathered hidden rows,
+ *   sorted_token [T*top_k] int32, the source token of each sorted row,
+ *   slot_pos [T*top_k] int32, the sorted row of (token t, slot j) at index t*top_k + j.
+ * Must be called with the scratch written by ggo_moe_route on the same stream. Deterministic
+ * (no atomics on positions): bit-exact against any stable counting sort. */
+int ggo_moe_permute(const void* x_dev, int64_t num_tokens, int64_t hidden, int num_experts,
+                    int top_k, const int32_t* topk_ids_dev, void* x_sorted_dev,
+                    int32_t* sorted_token_dev, int32_t* slot_pos_dev, void* scratch_dev,
+                    int dtype, cudaStream_t stream);
+
+/* Fused-MoE stage 4: top-k weighted combine.
+ *   out[t, :] = sum_{j < top_k} topk_weights[t, j] * y_sorted[slot_pos[t*top_k + j], :]
+ * accumulated in fp32 in fixed j order, rounded once to bf16/fp16. No atomics. */
+int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
+                    const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden, int top_k,
+                    void* out_dev, int dtype, cudaStream_t stream);
+
+/* Reads (and clears) the sticky device error of a workspace. Synchronises `stream`.
+ * Writes GGO_OK or a GGO_ERR_* code to *status_out. */
+int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGO_H_ */

@@ -1,0 +1,166 @@
+"""CPU oracle for the grouped-GEMM / fused-MoE hot path. TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may import this module, and
+only as the checker (or as the timed CPU baseline). The product path never calls it.
+
+What it restates, with the reference file:line each function follows (paths inside
+jeshxxx/GroupedGEMM-OPT):
+
+  sequential_gemm          benchmarks/benchmark.py:91-107  -- the reference's ground truth: a
+                           per-expert ``F.linear`` loop over expert-sorted row segments.
+  uniform_distribution     benchmarks/benchmark.py:50-56
+  skewed_distribution      benchmarks/benchmark.py:59-69
+  zipf_counts / dirichlet_counts   the seeded tpe generators of the BASELINE configs (cfg3), which
+                           the reference does not ship (its random_distribution,
+                           benchmark.py:72-79, is unseeded).
+  route / permute / combine / moe_layer   the fused-MoE layer. The reference has no router,
+                           permute or combine (its triton_fused_moe.py:81-101 gathers through an
+                           identity map), so these restate the conventions documented in
+                           grouped_gemm_opt/moe.py. Parity of these stages is UNPINNED (no
+                           reference implementation exists to pin against).
+
+Pinning: ``sequential_gemm`` and the two distribution generators are checked against golden
+vectors produced by the reference's own benchmark.py (tests/golden/make_golden.py imports it and
+commits small fixtures); see tests/test_oracle.py.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+
+# ----------------------------------------------------------------------------- grouped GEMM
+def sequential_gemm(input: torch.Tensor, weights: torch.Tensor,
+                    tokens_per_expert: torch.Tensor, out_dtype=None,
+                    native: bool = False) -> torch.Tensor:
+    """Per-expert loop (benchmark.py:91-107). Computes in fp32 from the given (bf16) values.
+
+    Returns fp32 unless ``out_dtype`` is given (the reference returns the input dtype, i.e. a
+    bf16 rounding of the same products: pass out_dtype=input.dtype for that).
+    ``native=True`` runs ``F.linear`` in the operands' own dtype exactly as the reference does
+    (used to time the reference algorithm as the CPU baseline)."""
+    x = input if native else input.float()
+    w = weights if native else weights.float()
+    outs = []
+    off = 0
+    for g in range(w.size(0)):
+        m = int(tokens_per_expert[g])
+        if m > 0:
+            outs.append(F.linear(x[off:off + m], w[g]))
+        off += m
+    out = torch.cat(outs, 0) if outs else torch.empty(0, w.size(1))
+    return out if out_dtype is None else out.to(out_dtype)
+
+
+def segments_gemm(input: torch.Tensor, weights: torch.Tensor, seg_counts: torch.Tensor,
+                  num_experts: int) -> torch.Tensor:
+    """Segment form: segment s multiplies by expert s % num_experts (fp32 result)."""
+    x = input.float()
+    w = weights.float()
+    out = torch.zeros(x.size(0), w.size(1))
+    off = 0
+    for s, m in enumerate(seg_counts.tolist()):
+        if m > 0:
+            out[off:off + m] = F.linear(x[off:off + m], w[s % num_experts])
+        off += m
+    return out
+
+
+def swiglu_gemm(x: torch.Tensor, w_gate_up: torch.Tensor, seg_counts: torch.Tensor,
+                num_experts: int) -> torch.Tensor:
+    """h = silu(x W_gate^T) * (x W_up^T) per segment; W_gu rows [0,F) gate, [F,2F) up. fp32."""
+    f = w_gate_up.size(1) // 2
+    gu = segments_gemm(x, w_gate_up, seg_counts, num_experts)
+    return F.silu(gu[:, :f]) * gu[:, f:]
+
+
+# ----------------------------------------------------------------------------- distributions
+def uniform_distribution(total_tokens: int, num_experts: int) -> torch.Tensor:
+    """benchmark.py:50-56: equal split, the remainder to the first experts."""
+    base, rem = divmod(total_tokens, num_experts)
+    tpe = torch.full((num_experts,), base, dtype=torch.int64)
+    tpe[:rem] += 1
+    return tpe
+
+
+def skewed_distribution(total_tokens: int, num_experts: int, skew_factor: float = 3.0):
+    """benchmark.py:59-69: power-law shares i^-skew, floored, rounding error to expert 0."""
+    w = torch.pow(torch.arange(1, num_experts + 1, dtype=torch.float64), -skew_factor)
+    w /= w.sum()
+    tpe = (w * total_tokens).long()
+    tpe[0] += total_tokens - int(tpe.sum())
+    return tpe
+
+
+def zipf_counts(total_tokens: int, num_experts: int, alpha: float = 1.2, seed: int = 0):
+    """cfg3 routing: multinomial(total, p_i ~ 1/(i+1)^alpha), seeded."""
+    g = torch.Generator().manual_seed(seed)
+    p = 1.0 / torch.arange(1, num_experts + 1, dtype=torch.float64) ** alpha
+    p /= p.sum()
+    draws = torch.multinomial(p, total_tokens, replacement=True, generator=g)
+    return torch.bincount(draws, minlength=num_experts).to(torch.int64)
+
+
+def dirichlet_counts(total_tokens: int, num_experts: int, alpha: float = 0.5, seed: int = 0):
+    """cfg3 'random' variant: Dirichlet(alpha) proportions, then a multinomial draw (numpy)."""
+    rng = np.random.default_rng(seed)
+    p = rng.dirichlet(np.full(num_experts, alpha))
+    return torch.from_numpy(rng.multinomial(total_tokens, p).astype(np.int64))
+
+
+# ----------------------------------------------------------------------------- fused MoE
+def route(logits: np.ndarray, top_k: int):
+    """Top-k (ties -> lower index) then softmax over the selected logits, fp32.
+    Returns ids int32 [T,k], weights fp32 [T,k], tokens_per_expert int64 [E]."""
+    lg = np.asarray(logits, dtype=np.float32)
+    T, E = lg.shape
+    order = np.argsort(-lg, axis=1, kind="stable")[:, :top_k]
+    vals = np.take_along_axis(lg, order, axis=1)
+    ex = np.exp(vals - vals[:, :1])
+    w = (ex / ex.sum(axis=1, keepdims=True)).astype(np.float32)
+    tpe = np.bincount(order.reshape(-1), minlength=E).astype(np.int64)
+    return order.astype(np.int32), w, tpe
+
+
+def permute_indices(ids: np.ndarray, num_experts: int):
+    """Stable counting sort of the (token, slot) entries by expert.
+    Returns sorted_token int32 [T*k] and slot_pos int32 [T*k] (index t*k+j -> sorted row)."""
+    flat = ids.reshape(-1).astype(np.int64)
+    order = np.argsort(flat, kind="stable")  # expert-major, then (t, j) order
+    k = ids.shape[1]
+    sorted_token = (order // k).astype(np.int32)
+    slot_pos = np.empty_like(order)
+    slot_pos[order] = np.arange(order.size)
+    return sorted_token, slot_pos.astype(np.int32)
+
+
+def combine(y_sorted: torch.Tensor, w: np.ndarray, slot_pos: np.ndarray) -> torch.Tensor:
+    """out[t] = sum_j w[t,j] * y_sorted[slot_pos[t*k+j]] in fp32, slot order."""
+    T, k = w.shape
+    y = y_sorted.float()
+    wt = torch.from_numpy(np.asarray(w, dtype=np.float32))
+    pos = torch.from_numpy(np.asarray(slot_pos, dtype=np.int64)).view(T, k)
+    out = torch.zeros(T, y.size(1))
+    for j in range(k):
+        out += wt[:, j:j + 1] * y[pos[:, j]]
+    return out
+
+
+def moe_layer(hidden: torch.Tensor, logits: torch.Tensor, w_gate_up: torch.Tensor,
+              w_down: torch.Tensor, top_k: int, round_to=None) -> torch.Tensor:
+    """Whole layer in fp32. With ``round_to`` (e.g. torch.bfloat16) the intermediate activations
+    (gathered rows, h, y) are rounded to that dtype as the GPU pipeline stores them."""
+    ids, w, tpe = route(logits.float().numpy(), top_k)
+    E = logits.size(1)
+    _, slot_pos = permute_indices(ids, E)
+    sorted_token, _ = permute_indices(ids, E)
+    xs = hidden[torch.from_numpy(sorted_token.astype(np.int64))]
+    counts = torch.from_numpy(tpe)
+    h = swiglu_gemm(xs, w_gate_up, counts, E)
+    if round_to is not None:
+        h = h.to(round_to)
+    y = segments_gemm(h, w_down, counts, E)
+    if round_to is not None:
+        y = y.to(round_to)
+    return combine(y, w, slot_pos)

@@ -1,0 +1,205 @@
+"""Parity of the tcgen05 grouped GEMM against the CPU oracle (the reference's per-expert
+sequential_gemm restated), on seeded inputs. All calls go through the C ABI (via the _C binding
+or directly through ctypes)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import grouped_gemm_oracle as oracle
+from gpu_util import assert_parity, reference_allclose
+from inputs import EDGE_CASES, cfg1_inputs, edge_inputs, gemm_inputs
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ggo():
+    import grouped_gemm_opt
+    return grouped_gemm_opt
+
+
+def test_cfg1_all_tile_configs(ggo):
+    x, w, tpe = cfg1_inputs()
+    ref = oracle.sequential_gemm(x, w, tpe)
+    xd, wd = x.to(DEV), w.to(DEV)
+    for tc in ggo.TileConfig:
+        for sort in (False, True):
+            out = ggo.grouped_gemm_opt(xd, wd, tpe, tc, sort_by_m=sort)
+            torch.cuda.synchronize()
+            assert out.shape == (256, 1024) and out.dtype == torch.bfloat16
+            assert_parity(out, ref, f"cfg1 tc={tc.name} sort={sort}")
+            assert reference_allclose(out, ref)
+
+
+def test_cfg1_gpu_counts_no_host_copy(ggo):
+    x, w, tpe = cfg1_inputs()
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV))
+    assert_parity(out, ref, "cfg1 gpu counts")
+    ggo.check_device_errors(0)
+
+
+@pytest.mark.parametrize("name", list(EDGE_CASES))
+@pytest.mark.parametrize("tc", [0, 1, 4])
+def test_edge_cases(ggo, name, tc):
+    x, w, tpe = edge_inputs(EDGE_CASES[name])
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
+    assert_parity(out, ref, f"{name} tc={tc}")
+    ggo.check_device_errors(0)
+
+
+@pytest.mark.parametrize("k,n", [(200, 1000), (8, 8), (4096, 136), (72, 520)])
+def test_odd_k_and_n(ggo, k, n):
+    x, w, tpe = gemm_inputs([3, 0, 130, 61, 1], k, n, seed=3)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    for tc in (0, 1):
+        out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe, tc)
+        assert_parity(out, ref, f"k={k} n={n} tc={tc}")
+
+
+def test_fp16(ggo):
+    x, w, tpe = gemm_inputs([17, 300, 0, 64], 256, 384, seed=5, dtype=torch.float16)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    for tc in (0, 1):
+        out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
+        assert out.dtype == torch.float16
+        assert_parity(out, ref, f"fp16 tc={tc}")
+        assert reference_allclose(out, ref, torch.float16)
+
+
+def test_many_experts_zero_counts(ggo):
+    tpe = oracle.dirichlet_counts(2048, 256, seed=1)
+    assert (tpe == 0).any()
+    x, w, _ = gemm_inputs(tpe, 256, 256, seed=7)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    for sort in (False, True):
+        out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), sort_by_m=sort)
+        assert_parity(out, ref, f"E=256 sort={sort}")
+
+
+def test_empty_input(ggo):
+    w = torch.randn(4, 64, 32, device=DEV, dtype=torch.bfloat16)
+    out = ggo.grouped_gemm_opt(torch.empty(0, 32, device=DEV, dtype=torch.bfloat16), w,
+                               torch.zeros(4, dtype=torch.int64))
+    assert out.shape == (0, 64)
+
+
+def test_count_mismatch(ggo):
+    x = torch.randn(10, 32, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(2, 64, 32, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        ggo.grouped_gemm_opt(x, w, torch.tensor([3, 4]))
+    ggo.grouped_gemm_opt(x, w, torch.tensor([3, 4], device=DEV))
+    with pytest.raises(RuntimeError):
+        ggo.check_device_errors(0)
+    ggo.check_device_errors(0)  # cleared
+
+
+def test_bad_arguments(ggo):
+    x = torch.randn(10, 30, device=DEV, dtype=torch.bfloat16)  # K not a multiple of 8
+    w = torch.randn(2, 64, 30, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        ggo.grouped_gemm_opt(x, w, torch.tensor([5, 5]))
+    with pytest.raises(RuntimeError):
+        ggo.grouped_gemm_opt(torch.randn(4, 32, device=DEV, dtype=torch.float32),
+                             torch.randn(1, 8, 32, device=DEV, dtype=torch.float32),
+                             torch.tensor([4]))
+    with pytest.raises(RuntimeError):  # K mismatch
+        ggo.grouped_gemm_opt(torch.randn(4, 32, device=DEV, dtype=torch.bfloat16),
+                             torch.randn(1, 8, 64, device=DEV, dtype=torch.bfloat16),
+                             torch.tensor([4]))
+
+
+def test_triton_aliases(ggo):
+    x, w, tpe = edge_inputs(EDGE_CASES["span_gt4"])
+    ref = oracle.sequential_gemm(x, w, tpe)
+    assert_parity(ggo.triton_fused_moe(x.to(DEV), w.to(DEV), tpe), ref, "triton_fused_moe")
+    assert_parity(ggo.triton_grouped_gemm(x.to(DEV), w.to(DEV), tpe, BLOCK_N=256), ref,
+                  "triton_grouped_gemm")
+
+
+def _sample_rows(tpe, per_expert=8, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    rows, off = [], 0
+    for m in tpe.tolist():
+        if m > 0:
+            rows.append(off + torch.randint(0, m, (min(per_expert, m),), generator=g))
+        off += m
+    return torch.cat(rows)
+
+
+def _ref_rows(x, w, tpe, rows):
+    """CPU fp32 reference for the sampled rows, one weight copy per expert touched."""
+    ex = torch.searchsorted(torch.cumsum(tpe, 0), rows, right=True)
+    xs = x[rows.to(x.device)].float().cpu()
+    ref = torch.empty(rows.numel(), w.size(1))
+    for e in ex.unique().tolist():
+        sel = (ex == e).nonzero().flatten()
+        ref[sel] = xs[sel] @ w[e].float().cpu().T
+    return ref
+
+
+@pytest.mark.parametrize("dist", ["uniform", "readme", "skewed"])
+def test_cfg2_full_size_sampled_rows(ggo, dist):
+    """cfg2 (E=8, T=4096, K=4096, N=14336) at full size; a row sample is checked on the CPU."""
+    T, E, K, N = 4096, 8, 4096, 14336
+    tpe = {"uniform": oracle.uniform_distribution(T, E),
+           "readme": torch.tensor([512, 480, 520, 500, 510, 490, 530, 554]),
+           "skewed": oracle.skewed_distribution(T, E)}[dist]
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    out = ggo.grouped_gemm_opt(x, w, tpe.to(DEV))
+    rows = _sample_rows(tpe)
+    ref = _ref_rows(x, w, tpe, rows)
+    assert_parity(out[rows.to(DEV)], ref, f"cfg2 {dist}")
+    ggo.check_device_errors(0)
+
+
+def test_cfg3_skewed_many_experts_sampled_rows(ggo):
+    T, E, K, N = 8192, 64, 4096, 14336
+    for tpe in (oracle.zipf_counts(T, E, seed=0), oracle.dirichlet_counts(T, E, seed=0)):
+        g = torch.Generator(device=DEV).manual_seed(1)
+        x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+        w = (torch.randn(E, N, K, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+        out = ggo.grouped_gemm_opt(x, w, tpe.to(DEV))
+        rows = _sample_rows(tpe, 4)
+        ref = _ref_rows(x, w, tpe, rows)
+        assert_parity(out[rows.to(DEV)], ref, "cfg3")
+        del w
+        torch.cuda.empty_cache()
+
+
+def test_c_abi_direct_ctypes():
+    """Calls ggo_grouped_gemm through ctypes with raw device pointers: no torch in the ABI."""
+    import grouped_gemm_opt  # noqa: F401  (initialises the CUDA context through torch)
+    from build_ext import lib_path
+    lib = ctypes.CDLL(str(lib_path()))
+    x, w, tpe = edge_inputs(EDGE_CASES["ragged"])
+    ref = oracle.sequential_gemm(x, w, tpe)
+    xd, wd, td = x.to(DEV), w.to(DEV), tpe.to(DEV)
+    out = torch.empty(x.size(0), w.size(1), device=DEV, dtype=torch.bfloat16)
+    lib.ggo_workspace_size.restype = ctypes.c_size_t
+    ws = torch.zeros(lib.ggo_workspace_size(), dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    f = lib.ggo_grouped_gemm
+    f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                          ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_void_p, ctypes.c_void_p]
+    for _ in range(2):
+        st = f(xd.data_ptr(), wd.data_ptr(), out.data_ptr(), td.data_ptr(), w.size(0), x.size(0),
+               w.size(1), w.size(2), 0, 4, 1, ws.data_ptr(), stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        assert_parity(out, ref, "ctypes")
+    code = ctypes.c_int(-1)
+    lib.ggo_workspace_error.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+    assert lib.ggo_workspace_error(ws.data_ptr(), stream, ctypes.byref(code)) == 0
+    assert code.value == 0
+    # the counters are back at zero after each launch
+    assert ws[:8].sum().item() == 0

@@ -1,0 +1,121 @@
+"""Fused-MoE stages on the GPU against the CPU oracle: router and permute bit-exact, SwiGLU
+gate/up and down GEMMs and the combine within the stated tolerance, and the whole layer."""
+import numpy as np
+import pytest
+import torch
+
+import grouped_gemm_oracle as oracle
+from gpu_util import assert_parity
+from inputs import gemm_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def C():
+    from grouped_gemm_opt import _C
+    return _C
+
+
+def _logits(T, E, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(T, E, generator=g)
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 8, 2), (300, 8, 2), (1000, 64, 6), (4096, 256, 8),
+                                   (129, 1024, 16), (257, 5, 5)])
+def test_route_and_permute_bit_exact(C, T, E, k):
+    logits = _logits(T, E, seed=T)
+    ids, w, tpe, scratch = C.moe_route(logits.to(DEV), k)
+    rid, rw, rtpe = oracle.route(logits.numpy(), k)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    assert np.array_equal(tpe.cpu().numpy(), rtpe)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    H = 64
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    xs, stok, spos = C.moe_permute(x.to(DEV), ids, scratch, E)
+    rst, rpos = oracle.permute_indices(rid, E)
+    assert np.array_equal(stok.cpu().numpy(), rst)
+    assert np.array_equal(spos.cpu().numpy(), rpos)
+    assert torch.equal(xs.cpu(), x[torch.from_numpy(rst).long()])
+
+
+def test_route_ties_lower_index(C):
+    logits = torch.zeros(3, 16)
+    logits[1, 7] = 1.0
+    ids, w, tpe, _ = C.moe_route(logits.to(DEV), 4)
+    assert ids.cpu().tolist() == [[0, 1, 2, 3], [7, 0, 1, 2], [0, 1, 2, 3]]
+
+
+@pytest.mark.parametrize("k", [1, 2, 8])
+def test_combine(C, k):
+    T, H = 333, 256
+    rng = np.random.default_rng(k)
+    ids = np.stack([rng.permutation(16)[:k] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    _, pos = oracle.permute_indices(ids, 16)
+    y = torch.randn(T * k, H, generator=torch.Generator().manual_seed(k)).to(torch.bfloat16)
+    out = C.moe_combine(y.to(DEV), torch.from_numpy(w).to(DEV), torch.from_numpy(pos).to(DEV))
+    ref = oracle.combine(y, w, pos)
+    # fp32 accumulation then one bf16 rounding: within 1 bf16 ulp of the fp32 oracle
+    diff = (out.float().cpu() - ref).abs()
+    assert (diff <= ref.abs() * 2.0 ** -8 + 1e-6).all(), diff.max()
+
+
+@pytest.mark.parametrize("counts,F,K", [([40, 0, 300, 7], 128, 256), ([5, 129, 1], 200, 64),
+                                        ([1000, 1000], 1024, 512)])
+def test_swiglu_gemm(C, counts, F, K):
+    x, w, tpe = gemm_inputs(counts, K, 2 * F, seed=11)
+    ref = oracle.swiglu_gemm(x, w, tpe, len(counts))
+    h = C.grouped_gemm_swiglu(x.to(DEV), w.to(DEV), tpe.to(DEV), len(counts), True)
+    assert h.shape == (x.size(0), F)
+    assert_parity(h, ref, "swiglu")
+
+
+def test_segments_layout_of_expert_parallel(C):
+    """Segments [src rank][local expert], segment s -> expert s % E_local (EP receive layout)."""
+    counts = [3, 0, 130, 17, 64, 1]  # 3 sources x 2 local experts
+    x, w, _ = gemm_inputs(counts, 128, 192, seed=4)
+    w = w[:2].contiguous()
+    tpe = torch.tensor(counts)
+    ref = oracle.segments_gemm(x, w, tpe, 2)
+    out = C.grouped_gemm_segments(x.to(DEV), w.to(DEV), tpe.to(DEV), 2, 4, True)
+    assert_parity(out, ref, "segments")
+
+
+def _moe_weights(E, H, F, seed):
+    g = torch.Generator().manual_seed(seed)
+    wgu = (torch.randn(E, 2 * F, H, generator=g) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(E, H, F, generator=g) * 0.02).to(torch.bfloat16)
+    return wgu, wd
+
+
+@pytest.mark.parametrize("T,H,F,E,k", [(512, 256, 512, 8, 2), (256, 1024, 512, 256, 8),
+                                       (77, 128, 64, 4, 1)])
+def test_fused_moe_small(T, H, F, E, k):
+    from grouped_gemm_opt import fused_moe
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g)
+    wgu, wd = _moe_weights(E, H, F, seed=E)
+    out = fused_moe(x.to(DEV), logits.to(DEV), wgu.to(DEV), wd.to(DEV), k)
+    ref = oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.bfloat16)
+    assert_parity(out, ref, "fused_moe")
+
+
+def test_fused_moe_mixtral_full_size_token_sample():
+    """Mixtral layer (T=16384, H=4096, F=14336, E=8, top-2) at full size; every token is
+    independent, so a token sample is checked against the oracle run on just those tokens."""
+    from grouped_gemm_opt import fused_moe
+    T, H, F, E, k = 16384, 4096, 14336, 8, 2
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, device=DEV, generator=g)
+    wgu = (torch.randn(E, 2 * F, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(E, H, F, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    out = fused_moe(x, logits, wgu, wd, k)
+    sel = torch.randperm(T, generator=torch.Generator().manual_seed(0))[:48]
+    ref = oracle.moe_layer(x[sel.to(DEV)].cpu(), logits[sel.to(DEV)].cpu(), wgu.cpu(), wd.cpu(),
+                           k, round_to=torch.bfloat16)
+    assert_parity(out[sel.to(DEV)], ref, "mixtral sample")
