@@ -163,10 +163,10 @@ def _timed(fn, steps, world):
     return total, [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
-def cpu_baseline_sample(threads: int):
+def cpu_baseline_sample(threads: int, min_s: float = 10.0):
     """The reference's algorithm (per-expert F.linear on bf16 CPU tensors, benchmark.py:91-107)
-    on a bounded sample of cfg2: the first expert's 512 rows (1/8 of the step), timed once
-    after one warm-up call. Returns TFLOP/s."""
+    on a bounded sample of cfg2: the first expert's 512 rows (1/8 of a step), repeated until at
+    least `min_s` seconds of CPU work, after one warm-up call. Returns (TFLOP/s, seconds, reps)."""
     import torch
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import grouped_gemm_oracle as oracle
@@ -177,10 +177,15 @@ def cpu_baseline_sample(threads: int):
     w = (torch.randn(1, N, K, generator=g) * 0.02).to(torch.bfloat16)
     tpe = torch.tensor([m])
     oracle.sequential_gemm(x[:64], w, torch.tensor([64]), native=True)
+    reps = 0
     t0 = time.perf_counter()
-    oracle.sequential_gemm(x, w, tpe, native=True)
-    dt = time.perf_counter() - t0
-    return 2.0 * m * N * K / dt / 1e12, dt
+    while True:
+        oracle.sequential_gemm(x, w, tpe, native=True)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_s:
+            break
+    return 2.0 * m * N * K * reps / dt / 1e12, dt, reps
 
 
 def run_reference(args):
@@ -189,9 +194,11 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    # every step is a bounded sample; keep the whole run within a few minutes
+    per_step_s = min(10.0, 120.0 / max(1, args.warmup + args.steps))
     vals = []
     for i in range(args.warmup + args.steps):
-        v, _ = cpu_baseline_sample(threads)
+        v, _, _ = cpu_baseline_sample(threads, per_step_s)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -239,7 +246,7 @@ def moe_layer_bench(world, rank, steps, warmup):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-moe", action="store_true")
@@ -268,6 +275,12 @@ def main():
     for _ in range(args.warmup):
         step()
     with ClockSampler(local) as clk:
+        # keep the GPU busy (untimed) while nvidia-smi starts, so its samples cover the load
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
         total_ms, per = _timed(step, args.steps, world)
     clocks = clk.summary()
     ms = total_ms / args.steps
@@ -294,8 +307,9 @@ def main():
 
     for _ in range(2):
         e2e_step()
-    e2e_ms, _ = _timed(e2e_step, max(3, args.steps // 2), world)
-    e2e_ms /= max(3, args.steps // 2)
+    n_e2e = max(3, min(200, args.steps // 10))
+    e2e_ms, _ = _timed(e2e_step, n_e2e, world)
+    e2e_ms /= n_e2e
     e2e = {"value": world * FLOP_PER_STEP / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
            "h2d_bytes_per_step": x.numel() * 2 + E * 8, "d2h_bytes_per_step": T_TOK * N * 2}
 
@@ -303,14 +317,15 @@ def main():
     if not args.no_moe:
         del out["y"]
         torch.cuda.empty_cache()
-        moe = moe_layer_bench(world, rank, max(3, args.steps // 4), 2)
+        moe = moe_layer_bench(world, rank, max(3, min(50, args.steps // 20)), 3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        v, dt = cpu_baseline_sample(threads)
+        v, dt, reps = cpu_baseline_sample(threads)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"first expert of cfg2 (512 rows, 60 GFLOP, bf16 F.linear), {dt:.1f} s"}
+               "sample": f"first expert of cfg2 (512 rows, 60 GFLOP, bf16 F.linear) x{reps}, "
+                         f"{dt:.1f} s"}
 
     if rank == 0:
         traffic = _traffic("grouped_gemm_cfg2")

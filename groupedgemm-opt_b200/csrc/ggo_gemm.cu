@@ -161,6 +161,28 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
 }
 
 }  // namespace
+
+// Scratch for ggo_grouped_gemm_noalloc: one workspace (tile counter, done counter, error word) in
+// a file-scope device array, so that entry point never allocates. Every GPU that loads this
+// library holds these 256 bytes until the process exits. Host code must not hand the symbol
+// itself to a kernel (on the host it only names a stand-in); the device address comes from
+// cudaGetSymbolAddress, looked up once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GGO_WORKSPACE_BYTES];
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+int noalloc_scratch(void** out) {
+  int dev;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GGO_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return GGO_ERR_CUDA;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GGO_OK;
+}
+
 }  // namespace ggo
 
 extern "C" {
@@ -212,6 +234,23 @@ int ggo_grouped_gemm_swiglu(const void* x_dev, const void* w_gate_up_dev, void* 
   return ggo::gemm_common(x_dev, w_gate_up_dev, h_dev, tokens_per_segment_dev, num_segments,
                           num_experts, total_tokens, F, K, dtype, GGO_TILE_AUTO, sort_by_m,
                           workspace_dev, stream, true);
+}
+
+int ggo_grouped_gemm_noalloc(const void* input_dev, const void* weights_dev, void* output_dev,
+                             const int64_t* tokens_per_expert_dev, int num_experts,
+                             int64_t total_tokens, int64_t N, int64_t K, int dtype,
+                             int tile_config, int sort_by_m, cudaStream_t stream) {
+  if (num_experts > GGO_NOALLOC_MAX_EXPERTS) return GGO_ERR_TOO_MANY_SEGMENTS;
+  if (!input_dev || !weights_dev || !output_dev || !tokens_per_expert_dev)
+    return GGO_ERR_INVALID_ARG;
+  void* scratch = nullptr;
+  if (int st = ggo::noalloc_scratch(&scratch)) return st;
+  // The array keeps whatever the previous call left; start every call from zero (stream-ordered,
+  // no allocation). This also discards any device-side error word of the previous call.
+  if (cudaMemsetAsync(scratch, 0, GGO_WORKSPACE_BYTES, stream) != cudaSuccess) return GGO_ERR_CUDA;
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_expert_dev, num_experts,
+                          num_experts, total_tokens, N, K, dtype, tile_config, sort_by_m, scratch,
+                          stream, false);
 }
 
 int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out) {

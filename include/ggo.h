@@ -140,6 +140,27 @@ int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
                     const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden, int top_k,
                     void* out_dev, int dtype, cudaStream_t stream);
 
+/* Grouped GEMM that allocates nothing: same arguments, result and validation as
+ * ggo_grouped_gemm, minus the workspace. It has no counterpart in the reference; it exists for
+ * callers that cannot call cudaMalloc themselves or hand over a buffer -- code running while a
+ * custom allocator must not be re-entered, plugins and hosts that give a kernel library no
+ * allocator, or code that owns no device memory at all.
+ * Its scratch is a fixed file-scope device array of GGO_WORKSPACE_BYTES (256 B) inside this
+ * library, held by every GPU that loads the library until the process exits. That scratch covers
+ * any problem with at most GGO_NOALLOC_MAX_EXPERTS experts; more experts are rejected with
+ * GGO_ERR_TOO_MANY_SEGMENTS. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture on that device.
+ * Every call shares the one array and clears it on `stream` before its launch, so calls that
+ * may overlap on the GPU (different streams, or other host threads) race and must be serialised
+ * by the caller. Device-side errors (count mismatch, bounded-wait timeout) are not reported by
+ * this entry point: the next call clears them. Calls no cudaMalloc, cudaFree or allocating
+ * library routine. */
+#define GGO_NOALLOC_MAX_EXPERTS GGO_MAX_SEGMENTS
+int ggo_grouped_gemm_noalloc(const void* input_dev, const void* weights_dev, void* output_dev,
+                             const int64_t* tokens_per_expert_dev, int num_experts,
+                             int64_t total_tokens, int64_t N, int64_t K, int dtype,
+                             int tile_config, int sort_by_m, cudaStream_t stream);
+
 /* Reads (and clears) the sticky device error of a workspace. Synchronises `stream`.
  * Writes GGO_OK or a GGO_ERR_* code to *status_out. */
 int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out);
