@@ -9,6 +9,7 @@
 
 #include "ggo.h"
 #include "ggo_gemm.cuh"
+#include "ggo_gemm_pair.cuh"
 #include "ggo_internal.h"
 
 namespace ggo {
@@ -25,6 +26,7 @@ EncodeTiledFn g_encode = nullptr;
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices] = {0};
 bool g_attr_done[kMaxDevices][8] = {{false}};
+int g_pair_clusters[kMaxDevices][4] = {{0}};  // co-resident CTA pairs per pair-kernel variant
 
 int get_encode(EncodeTiledFn* fn) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -82,6 +84,39 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 
+template <int EPI, bool BF16>
+int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
+                int slot, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  if (int st = make_map(&ma, a, p.rows, p.k, BF16)) return st;
+  if (int st = make_map(&mb, b, b_rows, p.k, BF16)) return st;
+  auto kern = grouped_gemm_pair_kernel<EPI, BF16>;
+  constexpr int smem = PairLayout::kTotal;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_pair_clusters[dev][slot] == 0) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return GGO_ERR_CUDA;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (g_sm_count[dev] / 2), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0)
+        return GGO_ERR_CUDA;
+      g_pair_clusters[dev][slot] = clusters;
+    }
+  }
+  constexpr int out_bn = (EPI == kEpiSwiGLU) ? 128 : 256;
+  const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
+  const int64_t ub = ((p.rows + 255) / 256 + p.num_segments) * n_tiles;  // pair-tile upper bound
+  const int64_t pairs = ub < g_pair_clusters[dev][slot] ? ub : g_pair_clusters[dev][slot];
+  if (pairs <= 0) return GGO_OK;
+  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+}
+
 int device_setup(int* dev_out) {
   int dev;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GGO_ERR_CUDA;
@@ -100,19 +135,25 @@ int device_setup(int* dev_out) {
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-int choose_bn(int tile_config, int64_t rows, int64_t n, int sms) {
+// Kernel choice: 128 = single-CTA 128x128 tile, 256 = single-CTA 128x256 tile,
+// 512 = CTA-pair 256x256 tile.
+int choose_bn(int tile_config, int64_t rows, int64_t n, int num_segments, int sms) {
   switch (tile_config) {
+    case GGO_TILE_PP_128x256x64:
+      return 512;
     case GGO_TILE_CO_128x128x64:
     case GGO_TILE_PP_128x128x128:
       return 128;
     case GGO_TILE_CO_128x256x64:
-    case GGO_TILE_PP_128x256x64:
       return 256;
-    default: {  // AUTO / CuBLAS_Seq: wide tiles unless they leave SMs idle
+    default: {  // AUTO / CuBLAS_Seq
       if (n <= 128) return 128;
       const int64_t m_tiles = (rows + kBM - 1) / kBM;
       const int64_t wide = m_tiles * ((n + 255) / 256);
-      return wide < sms ? 128 : 256;
+      if (wide < sms) return 128;            // narrow tiles keep every SM busy
+      // CTA pairs when segments average at least 192 rows (a 256-row tile is mostly full)
+      if (rows >= 192 * static_cast<int64_t>(num_segments) && wide / 2 >= sms) return 512;
+      return 256;
     }
   }
 }
@@ -148,11 +189,17 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.out = output;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
+  const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
   if (swiglu) {
+    if (bn == 512)
+      return bf16 ? launch_pair<kEpiSwiGLU, true>(input, weights, b_rows, p, dev, 2, stream)
+                  : launch_pair<kEpiSwiGLU, false>(input, weights, b_rows, p, dev, 3, stream);
     return bf16 ? launch<256, kEpiSwiGLU, true>(input, weights, b_rows, p, dev, 4, stream)
                 : launch<256, kEpiSwiGLU, false>(input, weights, b_rows, p, dev, 5, stream);
   }
-  const int bn = choose_bn(tile_config, rows, n, g_sm_count[dev]);
+  if (bn == 512)
+    return bf16 ? launch_pair<kEpiStore, true>(input, weights, b_rows, p, dev, 0, stream)
+                : launch_pair<kEpiStore, false>(input, weights, b_rows, p, dev, 1, stream);
   if (bn == 256)
     return bf16 ? launch<256, kEpiStore, true>(input, weights, b_rows, p, dev, 0, stream)
                 : launch<256, kEpiStore, false>(input, weights, b_rows, p, dev, 1, stream);

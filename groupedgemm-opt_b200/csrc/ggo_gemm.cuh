@@ -25,6 +25,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "ggo_ptx.cuh"
 
 namespace ggo {
@@ -92,65 +94,18 @@ struct SmemLayout {
   static constexpr int kTotal = 1024 /*align slack*/ + kTileBytes + kTableBytes + kMiscBytes;
 };
 
-template <int BN, int EPI, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-  using L = SmemLayout<BN>;
-  constexpr int S = L::kStages;
-  constexpr int kTmemCols = 2 * BN;             // two accumulators
-  constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
-
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* tiles = smem;
-  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
-  int* t_rowoff = t_cnt + kMaxSegments;
-  int* t_order = t_rowoff + kMaxSegments;
-  int* t_tileoff = t_order + kMaxSegments;  // kMaxSegments + 1 entries
-  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
-  uint64_t* empty_bar = full_bar + S;
-  uint64_t* accf_bar = empty_bar + S;
-  uint64_t* acce_bar = accf_bar + 2;
-  uint64_t* schf_bar = acce_bar + 2;
-  uint64_t* sche_bar = schf_bar + kSchedDepth;
-  TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
-
+// Builds, in shared memory, the segment table every CTA needs to map a flat tile index to work:
+// clamped counts, exclusive row offsets (segment order), processing order (identity or heaviest
+// first) and exclusive tile offsets (processing order); *total_tiles_s receives the tile count.
+// Called by all kThreads threads of the CTA (contains __syncthreads).
+template <int TILE_M, int OUT_BN>
+__device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t* tiles, int* t_cnt,
+                                                    int* t_rowoff, int* t_order, int* t_tileoff,
+                                                    int* total_tiles_s, int* err) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  int* err = &p.ws->error;
-
-  // ------------------------------------------------------------------ set-up
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&accf_bar[i], 1);
-      mbar_init(&acce_bar[i], 4);
-    }
-    for (int i = 0; i < kSchedDepth; ++i) {
-      mbar_init(&schf_bar[i], 1);
-      mbar_init(&sche_bar[i], 1 + 4);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-  }
-  if (warp == 2) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-
-  // Segment table, computed redundantly by every CTA from the device counts.
   const int nseg = p.num_segments;
+  // Segment table, computed redundantly by every CTA from the device counts.
   for (int s = threadIdx.x; s < nseg; s += kThreads) {
     long long c = p.counts[s];
     if (c < 0) {
@@ -210,12 +165,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = threadIdx.x; i < nseg; i += kThreads) t_order[i] = i;
   }
   __syncthreads();
-  const int n_tiles = (p.n_out + kOutBN - 1) / kOutBN;
+  const int n_tiles = (p.n_out + OUT_BN - 1) / OUT_BN;
   if (warp == 0) {  // exclusive prefix sum of tiles, in processing order
     int carry = 0;
     for (int base = 0; base < nseg; base += 32) {
       const int i = base + lane;
-      const int v = i < nseg ? ((t_cnt[t_order[i]] + kBM - 1) / kBM) * n_tiles : 0;
+      const int v = i < nseg ? ((t_cnt[t_order[i]] + TILE_M - 1) / TILE_M) * n_tiles : 0;
       int x = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -230,6 +185,179 @@ __global__ void __launch_bounds__(kThreads, 1)
       *total_tiles_s = carry;
     }
   }
+}
+
+// Maps flat tile index t (< total tiles) to its rows, output columns and weight rows.
+// Tiles of one segment are rastered in groups of kGroupM m-tiles: inside a group the m index
+// runs fastest, so concurrently running CTAs share the weight tile in L2.
+template <int TILE_M, int OUT_BN, int EPI>
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* t_cnt,
+                                                const int* t_rowoff, const int* t_order,
+                                                const int* t_tileoff) {
+  const int nseg = p.num_segments;
+  const int n_tiles = (p.n_out + OUT_BN - 1) / OUT_BN;
+  int lo = 0, hi = nseg - 1;  // last position whose tile offset is <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (t_tileoff[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int seg = t_order[lo];
+  const int local = t - t_tileoff[lo];
+  const int mt = (t_cnt[seg] + TILE_M - 1) / TILE_M;
+  const int group = local / (kGroupM * n_tiles);
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, mt - first_m);
+  const int r = local - group * kGroupM * n_tiles;
+  const int m_idx = first_m + r % gm;
+  const int n_idx = r / gm;
+  const int expert = seg % p.num_experts;
+  TileInfo info;
+  info.row0 = t_rowoff[seg] + m_idx * TILE_M;
+  info.rows = min(TILE_M, t_cnt[seg] - m_idx * TILE_M);
+  info.n0 = n_idx * OUT_BN;
+  if (EPI == kEpiSwiGLU) {
+    info.brow0 = expert * p.n_b + info.n0;                 // gate rows
+    info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
+  } else {
+    info.brow0 = expert * p.n_b + info.n0;
+    info.brow1 = info.brow0 + 128;
+  }
+  return info;
+}
+
+// Epilogue for one accumulator row held by this thread: TMEM columns [0, BN) of lane quarter
+// `t_row` -> (optional SwiGLU) -> bf16/fp16 -> 16-byte global stores of output columns
+// n0 + [0, BN or BN/2). All 32 lanes of the warp must call it (tcgen05.ld is warp-collective).
+template <int BN, int EPI, bool BF16, typename OutT>
+__device__ __forceinline__ void store_tile_row(uint32_t t_row, int n0, int n_out, bool row_ok,
+                                               OutT* out_row) {
+  if (EPI == kEpiStore) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_row + c, v);
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = n0 + c + 8 * j;
+          if (col < n_out) {
+            uint4 pk;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float a = __uint_as_float(v[8 * j + 2 * h]);
+              const float b = __uint_as_float(v[8 * j + 2 * h + 1]);
+              if (BF16) {
+                __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+                w[h] = *reinterpret_cast<uint32_t*>(&t2);
+              } else {
+                __half2 t2 = __floats2half2_rn(a, b);
+                w[h] = *reinterpret_cast<uint32_t*>(&t2);
+              }
+            }
+            *reinterpret_cast<uint4*>(out_row + col) = pk;
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(t_row + c, g);
+      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = n0 + c + 8 * j;
+          if (col < n_out) {
+            uint4 pk;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              float y[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const float gv = __uint_as_float(g[8 * j + 2 * h + e]);
+                const float uv = __uint_as_float(u[8 * j + 2 * h + e]);
+                y[e] = gv / (1.0f + __expf(-gv)) * uv;
+              }
+              if (BF16) {
+                __nv_bfloat162 t2 = __floats2bfloat162_rn(y[0], y[1]);
+                w[h] = *reinterpret_cast<uint32_t*>(&t2);
+              } else {
+                __half2 t2 = __floats2half2_rn(y[0], y[1]);
+                w[h] = *reinterpret_cast<uint32_t*>(&t2);
+              }
+            }
+            *reinterpret_cast<uint4*>(out_row + col) = pk;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int EPI, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using L = SmemLayout<BN>;
+  constexpr int S = L::kStages;
+  constexpr int kTmemCols = 2 * BN;             // two accumulators
+  constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
+  int* t_rowoff = t_cnt + kMaxSegments;
+  int* t_order = t_rowoff + kMaxSegments;
+  int* t_tileoff = t_order + kMaxSegments;  // kMaxSegments + 1 entries
+  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* accf_bar = empty_bar + S;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* schf_bar = acce_bar + 2;
+  uint64_t* sche_bar = schf_bar + kSchedDepth;
+  TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = &p.ws->error;
+
+  // ------------------------------------------------------------------ set-up
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf_bar[i], 1);
+      mbar_init(&acce_bar[i], 4);
+    }
+    for (int i = 0; i < kSchedDepth; ++i) {
+      mbar_init(&schf_bar[i], 1);
+      mbar_init(&sche_bar[i], 1 + 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+
+  build_segment_table<kBM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff, total_tiles_s, err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -245,33 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = atomicAdd(&p.ws->tile_counter, 1);
         TileInfo info;
         info.rows = 0;
-        if (t < total_tiles) {
-          int lo = 0, hi = nseg - 1;  // last position whose tile offset is <= t
-          while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (t_tileoff[mid] <= t) lo = mid; else hi = mid - 1;
-          }
-          const int seg = t_order[lo];
-          const int local = t - t_tileoff[lo];
-          const int mt = (t_cnt[seg] + kBM - 1) / kBM;
-          const int group = local / (kGroupM * n_tiles);
-          const int first_m = group * kGroupM;
-          const int gm = min(kGroupM, mt - first_m);
-          const int r = local - group * kGroupM * n_tiles;
-          const int m_idx = first_m + r % gm;
-          const int n_idx = r / gm;
-          const int expert = seg % p.num_experts;
-          info.row0 = t_rowoff[seg] + m_idx * kBM;
-          info.rows = min(kBM, t_cnt[seg] - m_idx * kBM);
-          info.n0 = n_idx * kOutBN;
-          if (EPI == kEpiSwiGLU) {
-            info.brow0 = expert * p.n_b + info.n0;              // gate rows
-            info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
-          } else {
-            info.brow0 = expert * p.n_b + info.n0;
-            info.brow1 = info.brow0 + 128;
-          }
-        }
+        if (t < total_tiles) info = decode_tile<kBM, kOutBN, EPI>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);
@@ -351,73 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       OutT* out_row = reinterpret_cast<OutT*>(p.out) +
                       static_cast<size_t>(info.row0 + r_local) * p.n_out;
-      if (EPI == kEpiStore) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + c, v);
-          tmem_ld_wait();
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = info.n0 + c + 8 * j;
-              if (col < p.n_out) {
-                uint4 pk;
-                uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  const float a = __uint_as_float(v[8 * j + 2 * h]);
-                  const float b = __uint_as_float(v[8 * j + 2 * h + 1]);
-                  if (BF16) {
-                    __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
-                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
-                  } else {
-                    __half2 t2 = __floats2half2_rn(a, b);
-                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
-                  }
-                }
-                *reinterpret_cast<uint4*>(out_row + col) = pk;
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(t_row + c, g);
-          tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
-          tmem_ld_wait();
-          if (row_ok) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = info.n0 + c + 8 * j;
-              if (col < p.n_out) {
-                uint4 pk;
-                uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  float y[2];
-#pragma unroll
-                  for (int e = 0; e < 2; ++e) {
-                    const float gv = __uint_as_float(g[8 * j + 2 * h + e]);
-                    const float uv = __uint_as_float(u[8 * j + 2 * h + e]);
-                    y[e] = gv / (1.0f + __expf(-gv)) * uv;
-                  }
-                  if (BF16) {
-                    __nv_bfloat162 t2 = __floats2bfloat162_rn(y[0], y[1]);
-                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
-                  } else {
-                    __half2 t2 = __floats2half2_rn(y[0], y[1]);
-                    w[h] = *reinterpret_cast<uint32_t*>(&t2);
-                  }
-                }
-                *reinterpret_cast<uint4*>(out_row + col) = pk;
-              }
-            }
-          }
-        }
-      }
+      store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);

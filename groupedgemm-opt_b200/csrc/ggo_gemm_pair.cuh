@@ -1,0 +1,231 @@
+// CTA-pair (cta_group::2) variant of the persistent grouped GEMM: 256 x 256 output tiles.
+//
+// A cluster of two CTAs on two SMs computes one 256-row tile. Each CTA TMA-loads its own 128 A
+// rows and its own half (128 rows) of the B tile; one thread of the even CTA issues
+// tcgen05.mma.cta_group::2 with M = 256, which reads A and the B halves from both CTAs' shared
+// memory and accumulates each CTA's 128 rows into that CTA's TMEM. Per SM this moves 32 KB per
+// 64-deep K step instead of 48 KB for a 128 x 256 single-CTA tile: the L2 -> SM operand traffic
+// that bounds the single-CTA kernel drops by a third.
+//
+// There is NO TMA multicast: every load lands in the issuing CTA's own shared memory; only its
+// completion is counted on the leader's barrier (the cta_group::2 form of the bulk-tensor load).
+// tcgen05.commit with .multicast::cluster signals both CTAs' barriers when MMAs retire.
+//
+// Scheduling: the leader's producer claims a tile from the global atomic counter, decodes it and
+// writes it into both CTAs' tile rings (distributed shared memory). Consumers of a ring slot in
+// both CTAs release it on the leader's barrier.
+#pragma once
+
+#include "ggo_gemm.cuh"
+
+namespace ggo {
+
+struct PairLayout {
+  static constexpr int kStages = 6;
+  static constexpr int kABytes = 128 * kBK * 2;  // this CTA's 128 A rows
+  static constexpr int kBBytes = 128 * kBK * 2;  // this CTA's half of the 256-row B tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTileBytes = kStages * kStageBytes;
+  static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
+  static constexpr int kMiscBytes = 1024;
+  static constexpr int kTotal = 1024 + kTileBytes + kTableBytes + kMiscBytes;
+};
+
+template <int EPI, bool BF16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using L = PairLayout;
+  constexpr int S = L::kStages;
+  constexpr int BN = 256;                // N of the pair tile = columns of each CTA's accumulator
+  constexpr int kTileM = 256;
+  constexpr int kTmemCols = 2 * BN;      // two accumulators
+  constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
+  int* t_rowoff = t_cnt + kMaxSegments;
+  int* t_order = t_rowoff + kMaxSegments;
+  int* t_tileoff = t_order + kMaxSegments;
+  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* accf_bar = empty_bar + S;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* schf_bar = acce_bar + 2;
+  uint64_t* sche_bar = schf_bar + kSchedDepth;
+  TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  int* err = &p.ws->error;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);    // leader: its expect_tx arrive + both CTAs' bytes
+      mbar_init(&empty_bar[i], 1);   // both: one multicast commit per use
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf_bar[i], 1);    // both: one multicast commit per tile
+      mbar_init(&acce_bar[i], 8);    // leader: 4 epilogue warps x 2 CTAs
+    }
+    for (int i = 0; i < kSchedDepth; ++i) {
+      mbar_init(&schf_bar[i], 1);              // both: the leader producer
+      mbar_init(&sche_bar[i], 1 + 4 + 1 + 4);  // leader: MMA, 4+4 epilogue warps, peer producer
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  build_segment_table<kTileM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff,
+                                      total_tiles_s, err);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = *total_tiles_s;
+  const int num_kb = (p.k + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- TMA producers (both CTAs)
+    if (lane == 0) {
+      int stage = 0, phase = 0, q = 0, qphase = 0;
+      while (true) {
+        TileInfo info;
+        if (leader) {
+          const int t = atomicAdd(&p.ws->tile_counter, 1);
+          info.rows = 0;
+          if (t < total_tiles)
+            info = decode_tile<kTileM, kOutBN, EPI>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+          if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer))
+            break;
+          ring[q] = info;
+          const uint32_t pr = mapa_shared(&ring[q], 1);
+          st_cluster_v4(pr, info.row0, info.rows, info.n0, info.brow0);
+          st_cluster_v4(pr + 16, info.brow1, 0, 0, 0);
+          mbar_arrive(&schf_bar[q]);
+          mbar_arrive_cluster(mapa_shared(&schf_bar[q], 1));
+        } else {
+          if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutProducer))
+            break;
+          info = ring[q];
+          mbar_arrive_cluster(mapa_shared(&sche_bar[q], 0));
+        }
+        if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+        if (info.rows == 0) break;
+        const int a_row = info.row0 + static_cast<int>(rank) * 128;
+        const int b_row = leader ? info.brow0 : info.brow1;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, abort_flag, err,
+                                 kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = tiles + stage * L::kStageBytes;
+          uint8_t* b_dst = a_dst + L::kABytes;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+          const uint32_t fb = mapa_shared(&full_bar[stage], 0);
+          tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, a_row);
+          tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kTileM, BN, BF16);
+      int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
+      const uint32_t tiles_addr = smem_u32(tiles);
+      while (true) {
+        if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutMma)) break;
+        const bool valid = ring[q].rows > 0;
+        mbar_arrive(&sche_bar[q]);
+        if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+        if (!valid) break;
+        if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, abort_flag, err, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(&full_bar[stage], phase, abort_flag, err, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = tiles_addr + stage * L::kStageBytes;
+          const uint64_t adesc = sdesc_sw128_kmajor(a_addr);
+          const uint64_t bdesc = sdesc_sw128_kmajor(a_addr + L::kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          mma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit_pair(&accf_bar[acc], 0x3);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int ew = warp - 4;
+    int q = 0, qphase = 0, acc = 0, aphase = 0;
+    using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    while (true) {
+      if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      const TileInfo info = ring[q];
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&sche_bar[q], 0));
+      if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
+      if (info.rows == 0) break;
+      if (!mbar_wait_cluster(&accf_bar[acc], aphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int r_local = static_cast<int>(rank) * 128 + ew * 32 + lane;
+      const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
+      OutT* out_row = reinterpret_cast<OutT*>(p.out) +
+                      static_cast<size_t>(info.row0 + r_local) * p.n_out;
+      store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));
+      if (++acc == 2) { acc = 0; aphase ^= 1; }
+    }
+  }
+
+  // ------------------------------------------------------------------ tear-down
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no remote arrive or ring store may target a CTA that has exited
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&p.ws->done_counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(&p.ws->tile_counter, 0);
+      atomicExch(&p.ws->done_counter, 0);
+    }
+  }
+}
+
+}  // namespace ggo

@@ -44,7 +44,7 @@ def test_cfg1_gpu_counts_no_host_copy(ggo):
 
 
 @pytest.mark.parametrize("name", list(EDGE_CASES))
-@pytest.mark.parametrize("tc", [0, 1, 4])
+@pytest.mark.parametrize("tc", [0, 1, 3, 4])
 def test_edge_cases(ggo, name, tc):
     x, w, tpe = edge_inputs(EDGE_CASES[name])
     ref = oracle.sequential_gemm(x, w, tpe)
@@ -57,7 +57,7 @@ def test_edge_cases(ggo, name, tc):
 def test_odd_k_and_n(ggo, k, n):
     x, w, tpe = gemm_inputs([3, 0, 130, 61, 1], k, n, seed=3)
     ref = oracle.sequential_gemm(x, w, tpe)
-    for tc in (0, 1):
+    for tc in (0, 1, 3):
         out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe, tc)
         assert_parity(out, ref, f"k={k} n={n} tc={tc}")
 
@@ -65,7 +65,7 @@ def test_odd_k_and_n(ggo, k, n):
 def test_fp16(ggo):
     x, w, tpe = gemm_inputs([17, 300, 0, 64], 256, 384, seed=5, dtype=torch.float16)
     ref = oracle.sequential_gemm(x, w, tpe)
-    for tc in (0, 1):
+    for tc in (0, 1, 3):
         out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
         assert out.dtype == torch.float16
         assert_parity(out, ref, f"fp16 tc={tc}")
@@ -78,8 +78,9 @@ def test_many_experts_zero_counts(ggo):
     x, w, _ = gemm_inputs(tpe, 256, 256, seed=7)
     ref = oracle.sequential_gemm(x, w, tpe)
     for sort in (False, True):
-        out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), sort_by_m=sort)
-        assert_parity(out, ref, f"E=256 sort={sort}")
+        for tc in (4, 3):
+            out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc, sort_by_m=sort)
+            assert_parity(out, ref, f"E=256 sort={sort} tc={tc}")
 
 
 def test_empty_input(ggo):
@@ -144,8 +145,9 @@ def _ref_rows(x, w, tpe, rows):
     return ref
 
 
+@pytest.mark.parametrize("tc", [4, 1])
 @pytest.mark.parametrize("dist", ["uniform", "readme", "skewed"])
-def test_cfg2_full_size_sampled_rows(ggo, dist):
+def test_cfg2_full_size_sampled_rows(ggo, dist, tc):
     """cfg2 (E=8, T=4096, K=4096, N=14336) at full size; a row sample is checked on the CPU."""
     T, E, K, N = 4096, 8, 4096, 14336
     tpe = {"uniform": oracle.uniform_distribution(T, E),
@@ -154,10 +156,10 @@ def test_cfg2_full_size_sampled_rows(ggo, dist):
     g = torch.Generator(device=DEV).manual_seed(0)
     x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
     w = (torch.randn(E, N, K, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
-    out = ggo.grouped_gemm_opt(x, w, tpe.to(DEV))
+    out = ggo.grouped_gemm_opt(x, w, tpe.to(DEV), tc)
     rows = _sample_rows(tpe)
     ref = _ref_rows(x, w, tpe, rows)
-    assert_parity(out[rows.to(DEV)], ref, f"cfg2 {dist}")
+    assert_parity(out[rows.to(DEV)], ref, f"cfg2 {dist} tc={tc}")
     ggo.check_device_errors(0)
 
 
