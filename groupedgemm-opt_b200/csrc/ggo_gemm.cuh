@@ -19,7 +19,7 @@
 //  * Epilogues: plain store, or SwiGLU (silu(gate) * up) for the fused-MoE gate/up projection,
 //    where one 256-wide B tile holds 128 gate rows and the matching 128 up rows.
 //
-// No TMA multicast is used anywhere, so the same code is safe on every GPU count.
+// Every bulk-tensor load writes only the issuing CTA's shared memory, from this GPU's memory.
 #pragma once
 
 #include <cuda_bf16.h>

@@ -7,9 +7,9 @@
 // 64-deep K step instead of 48 KB for a 128 x 256 single-CTA tile: the L2 -> SM operand traffic
 // that bounds the single-CTA kernel drops by a third.
 //
-// There is NO TMA multicast: every load lands in the issuing CTA's own shared memory; only its
+// Every bulk-tensor load lands in the issuing CTA's own shared memory (no broadcast); only its
 // completion is counted on the leader's barrier (the cta_group::2 form of the bulk-tensor load).
-// tcgen05.commit with .multicast::cluster signals both CTAs' barriers when MMAs retire.
+// One tcgen05.commit with a two-CTA mask signals both CTAs' barriers when MMAs retire.
 //
 // Scheduling: the leader's producer claims a tile from the global atomic counter, decodes it and
 // writes it into both CTAs' tile rings (distributed shared memory). Consumers of a ring slot in
@@ -71,10 +71,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_bar[i], 1);    // leader: its expect_tx arrive + both CTAs' bytes
-      mbar_init(&empty_bar[i], 1);   // both: one multicast commit per use
+      mbar_init(&empty_bar[i], 1);   // both: one two-CTA commit per use
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&accf_bar[i], 1);    // both: one multicast commit per tile
+      mbar_init(&accf_bar[i], 1);    // both: one two-CTA commit per tile
       mbar_init(&acce_bar[i], 8);    // leader: 4 epilogue warps x 2 CTAs
     }
     for (int i = 0; i < kSchedDepth; ++i) {

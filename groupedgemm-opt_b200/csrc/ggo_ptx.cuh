@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the grouped-GEMM kernels use:
-// mbarriers, TMA tiled loads (no cluster multicast anywhere), and the tcgen05
+// mbarriers, TMA tiled loads (each into the issuing CTA only), and the tcgen05
 // tensor-core family (TMEM alloc/dealloc, MMA, commit, TMEM -> register loads).
 //
 // Every wait in this library is bounded: `mbar_wait` gives up after
@@ -224,7 +224,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // 2D tiled load into this CTA's shared memory whose completion is counted on the mbarrier at
-// `bar_cluster` (a shared::cluster address, here the pair leader's barrier). No multicast.
+// `bar_cluster` (a shared::cluster address, here the pair leader's barrier).
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm,
                                                  uint32_t bar_cluster, int x, int y) {
   asm volatile(
