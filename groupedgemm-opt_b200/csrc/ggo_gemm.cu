@@ -5,6 +5,8 @@
 // (launch_grouped_gemm). Differences by design: the token counts stay on the device (no
 // cudaStreamSynchronize), zero-token experts are skipped inside the kernel, and there is no
 // per-group argument buffer to build or copy.
+#include <cstdlib>
+#include <map>
 #include <mutex>
 
 #include "ggo.h"
@@ -25,8 +27,6 @@ std::mutex g_mu;
 EncodeTiledFn g_encode = nullptr;
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices] = {0};
-bool g_attr_done[kMaxDevices][8] = {{false}};
-int g_pair_clusters[kMaxDevices][4] = {{0}};  // co-resident CTA pairs per pair-kernel variant
 
 int get_encode(EncodeTiledFn* fn) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -43,13 +43,14 @@ int get_encode(EncodeTiledFn* fn) {
   return GGO_OK;
 }
 
-// 2D K-major operand map: dims {K, rows}, box {64, 128}, 128-B swizzle, zero fill out of bounds.
-int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16) {
+// 2D K-major operand map: dims {K, rows}, box {64, box_rows}, 128-B swizzle, zero fill out of
+// bounds.
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows) {
   EncodeTiledFn enc;
   if (int st = get_encode(&enc)) return st;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), 128};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                    const_cast<void*>(base), dims, strides, box, estr,
@@ -58,64 +59,121 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf1
   return r == CUDA_SUCCESS ? GGO_OK : GGO_ERR_CUDA;
 }
 
+// Per (device, kernel) one-time set-up: the dynamic shared-memory opt-in and, for cluster
+// kernels, how many clusters can be resident at once.
+std::map<std::pair<int, const void*>, int> g_kernel_slots;
+
+template <typename Kern>
+int kernel_setup(Kern kern, int smem, int dev, bool pair, int* resident) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
+  auto it = g_kernel_slots.find(key);
+  if (it == g_kernel_slots.end()) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return GGO_ERR_CUDA;
+    int n = g_sm_count[dev];
+    if (pair) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (g_sm_count[dev] / 2), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = smem;
+      n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
+        return GGO_ERR_CUDA;
+    }
+    it = g_kernel_slots.emplace(key, n).first;
+  }
+  *resident = it->second;
+  return GGO_OK;
+}
+
 template <int BN, int EPI, bool BF16>
-int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev, int slot,
+int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
            cudaStream_t stream) {
   CUtensorMap ma, mb;
-  if (int st = make_map(&ma, a, p.rows, p.k, BF16)) return st;
-  if (int st = make_map(&mb, b, b_rows, p.k, BF16)) return st;
+  if (int st = make_map(&ma, a, p.rows, p.k, BF16, kBM)) return st;
+  if (int st = make_map(&mb, b, b_rows, p.k, BF16, 128)) return st;
   auto kern = grouped_gemm_kernel<BN, EPI, BF16>;
   constexpr int smem = SmemLayout<BN>::kTotal;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_attr_done[dev][slot]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-          cudaSuccess)
-        return GGO_ERR_CUDA;
-      g_attr_done[dev][slot] = true;
-    }
-  }
+  int sms = 0;
+  if (int st = kernel_setup(kern, smem, dev, false, &sms)) return st;
   constexpr int out_bn = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
   const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
   const int64_t ub = ((p.rows + kBM - 1) / kBM + p.num_segments) * n_tiles;  // tile upper bound
-  const int grid = static_cast<int>(ub < g_sm_count[dev] ? ub : g_sm_count[dev]);
+  const int grid = static_cast<int>(ub < sms ? ub : sms);
   if (grid <= 0) return GGO_OK;
   kern<<<grid, kThreads, smem, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 
-template <int EPI, bool BF16>
+template <int BN, int EPI, bool BF16>
 int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
-                int slot, cudaStream_t stream) {
+                cudaStream_t stream) {
   CUtensorMap ma, mb;
-  if (int st = make_map(&ma, a, p.rows, p.k, BF16)) return st;
-  if (int st = make_map(&mb, b, b_rows, p.k, BF16)) return st;
-  auto kern = grouped_gemm_pair_kernel<EPI, BF16>;
-  constexpr int smem = PairLayout::kTotal;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (g_pair_clusters[dev][slot] == 0) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-          cudaSuccess)
-        return GGO_ERR_CUDA;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * (g_sm_count[dev] / 2), 1, 1);
-      cfg.blockDim = dim3(kThreads, 1, 1);
-      cfg.dynamicSmemBytes = smem;
-      int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0)
-        return GGO_ERR_CUDA;
-      g_pair_clusters[dev][slot] = clusters;
-    }
-  }
-  constexpr int out_bn = (EPI == kEpiSwiGLU) ? 128 : 256;
+  if (int st = make_map(&ma, a, p.rows, p.k, BF16, 128)) return st;
+  if (int st = make_map(&mb, b, b_rows, p.k, BF16, BN / 2)) return st;
+  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16>;
+  constexpr int smem = PairLayout<BN>::kTotal;
+  int clusters = 0;
+  if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
+  constexpr int out_bn = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
   const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
   const int64_t ub = ((p.rows + 255) / 256 + p.num_segments) * n_tiles;  // pair-tile upper bound
-  const int64_t pairs = ub < g_pair_clusters[dev][slot] ? ub : g_pair_clusters[dev][slot];
+  const int64_t pairs = ub < clusters ? ub : clusters;
   if (pairs <= 0) return GGO_OK;
   kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
+
+// Pair-tile width: the candidate that minimises (waves of tiles over the resident pairs) x (tile
+// width + a fixed per-tile overhead), with the m-tile count estimated from evenly split segments
+// (the counts themselves stay on the device).
+int choose_pair_bn(int64_t rows, int64_t n_out, int num_segments, bool swiglu, int pairs) {
+  static const int kPlain[] = {256, 224, 192, 160};
+  static const int kGlu[] = {256, 192, 128};
+  const int* cand = swiglu ? kGlu : kPlain;
+  const int nc = swiglu ? 3 : 4;
+  const int64_t per_seg = (rows + num_segments - 1) / num_segments;
+  int64_t mt = num_segments * ((per_seg + 255) / 256);
+  const int64_t mt_min = (rows + 255) / 256;
+  if (mt < mt_min) mt = mt_min;
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int i = 0; i < nc; ++i) {
+    const int out = swiglu ? cand[i] / 2 : cand[i];
+    const int64_t tiles = mt * ((n_out + out - 1) / out);
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    const int64_t cost = waves * (cand[i] + 16);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = cand[i];
+    }
+  }
+  return best;
+}
+
+template <int EPI, bool BF16>
+int launch_pair_bn(int bn, const void* a, const void* b, int64_t b_rows, const GemmParams& p,
+                   int dev, cudaStream_t stream) {
+  switch (bn) {
+    case 224: if constexpr (EPI == kEpiStore) return launch_pair<224, EPI, BF16>(a, b, b_rows, p, dev, stream); break;
+    case 192: return launch_pair<192, EPI, BF16>(a, b, b_rows, p, dev, stream);
+    case 160: if constexpr (EPI == kEpiStore) return launch_pair<160, EPI, BF16>(a, b, b_rows, p, dev, stream); break;
+    case 128: return launch_pair<128, EPI, BF16>(a, b, b_rows, p, dev, stream);
+    default: break;
+  }
+  return launch_pair<256, EPI, BF16>(a, b, b_rows, p, dev, stream);
+}
+
+// Tuning knobs, read on every call (cheap next to a launch): GGO_RASTER_GROUP_M (m-tiles per
+// raster group, default 8) and GGO_PAIR_BN (force the CTA-pair tile width: 256/224/192/160/128).
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  const int v = e ? atoi(e) : 0;
+  return v > 0 ? v : dflt;
+}
+int raster_group_m() { return env_int("GGO_RASTER_GROUP_M", 8); }
 
 int device_setup(int* dev_out) {
   int dev;
@@ -186,25 +244,28 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.n_b = static_cast<int>(swiglu ? 2 * n : n);
   p.k = static_cast<int>(k);
   p.sort_by_m = sort_by_m ? 1 : 0;
+  p.group_m = raster_group_m();
   p.out = output;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
-  if (swiglu) {
-    if (bn == 512)
-      return bf16 ? launch_pair<kEpiSwiGLU, true>(input, weights, b_rows, p, dev, 2, stream)
-                  : launch_pair<kEpiSwiGLU, false>(input, weights, b_rows, p, dev, 3, stream);
-    return bf16 ? launch<256, kEpiSwiGLU, true>(input, weights, b_rows, p, dev, 4, stream)
-                : launch<256, kEpiSwiGLU, false>(input, weights, b_rows, p, dev, 5, stream);
+  if (bn == 512) {
+    const int pbn = env_int("GGO_PAIR_BN",
+                            choose_pair_bn(rows, n, num_segments, swiglu, g_sm_count[dev] / 2));
+    if (swiglu)
+      return bf16 ? launch_pair_bn<kEpiSwiGLU, true>(pbn, input, weights, b_rows, p, dev, stream)
+                  : launch_pair_bn<kEpiSwiGLU, false>(pbn, input, weights, b_rows, p, dev, stream);
+    return bf16 ? launch_pair_bn<kEpiStore, true>(pbn, input, weights, b_rows, p, dev, stream)
+                : launch_pair_bn<kEpiStore, false>(pbn, input, weights, b_rows, p, dev, stream);
   }
-  if (bn == 512)
-    return bf16 ? launch_pair<kEpiStore, true>(input, weights, b_rows, p, dev, 0, stream)
-                : launch_pair<kEpiStore, false>(input, weights, b_rows, p, dev, 1, stream);
+  if (swiglu)
+    return bf16 ? launch<256, kEpiSwiGLU, true>(input, weights, b_rows, p, dev, stream)
+                : launch<256, kEpiSwiGLU, false>(input, weights, b_rows, p, dev, stream);
   if (bn == 256)
-    return bf16 ? launch<256, kEpiStore, true>(input, weights, b_rows, p, dev, 0, stream)
-                : launch<256, kEpiStore, false>(input, weights, b_rows, p, dev, 1, stream);
-  return bf16 ? launch<128, kEpiStore, true>(input, weights, b_rows, p, dev, 2, stream)
-              : launch<128, kEpiStore, false>(input, weights, b_rows, p, dev, 3, stream);
+    return bf16 ? launch<256, kEpiStore, true>(input, weights, b_rows, p, dev, stream)
+                : launch<256, kEpiStore, false>(input, weights, b_rows, p, dev, stream);
+  return bf16 ? launch<128, kEpiStore, true>(input, weights, b_rows, p, dev, stream)
+              : launch<128, kEpiStore, false>(input, weights, b_rows, p, dev, stream);
 }
 
 }  // namespace

@@ -37,7 +37,6 @@ constexpr int kUmmaK = 16;        // K per tcgen05.mma kind::f16
 constexpr int kMaxSegments = 1024;
 constexpr int kSchedDepth = 4;
 constexpr int kThreads = 256;
-constexpr int kGroupM = 16;       // m-tiles per raster group (L2 reuse of the weight tile)
 
 enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1 };
 
@@ -69,6 +68,7 @@ struct GemmParams {
   int n_b;                // rows of one expert's W (N, or 2F for SwiGLU)
   int k;                  // K
   int sort_by_m;          // process segments heaviest-first
+  int group_m;            // m-tiles per raster group (>= 1)
   void* out;              // [rows, n_out], bf16 or fp16
   GgoWorkspace* ws;
 };
@@ -188,9 +188,9 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
 }
 
 // Maps flat tile index t (< total tiles) to its rows, output columns and weight rows.
-// Tiles of one segment are rastered in groups of kGroupM m-tiles: inside a group the m index
+// Tiles of one segment are rastered in groups of p.group_m m-tiles: inside a group the m index
 // runs fastest, so concurrently running CTAs share the weight tile in L2.
-template <int TILE_M, int OUT_BN, int EPI>
+template <int TILE_M, int OUT_BN, int EPI, int B_HALF>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* t_cnt,
                                                 const int* t_rowoff, const int* t_order,
                                                 const int* t_tileoff) {
@@ -204,10 +204,11 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
   const int seg = t_order[lo];
   const int local = t - t_tileoff[lo];
   const int mt = (t_cnt[seg] + TILE_M - 1) / TILE_M;
-  const int group = local / (kGroupM * n_tiles);
-  const int first_m = group * kGroupM;
-  const int gm = min(kGroupM, mt - first_m);
-  const int r = local - group * kGroupM * n_tiles;
+  const int gsz = p.group_m;
+  const int group = local / (gsz * n_tiles);
+  const int first_m = group * gsz;
+  const int gm = min(gsz, mt - first_m);
+  const int r = local - group * gsz * n_tiles;
   const int m_idx = first_m + r % gm;
   const int n_idx = r / gm;
   const int expert = seg % p.num_experts;
@@ -220,7 +221,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
   } else {
     info.brow0 = expert * p.n_b + info.n0;
-    info.brow1 = info.brow0 + 128;
+    info.brow1 = info.brow0 + B_HALF;  // second half of the B tile
   }
   return info;
 }
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = atomicAdd(&p.ws->tile_counter, 1);
         TileInfo info;
         info.rows = 0;
-        if (t < total_tiles) info = decode_tile<kBM, kOutBN, EPI>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+        if (t < total_tiles) info = decode_tile<kBM, kOutBN, EPI, 128>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);

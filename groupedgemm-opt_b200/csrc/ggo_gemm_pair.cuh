@@ -20,26 +20,29 @@
 
 namespace ggo {
 
+template <int BN>
 struct PairLayout {
-  static constexpr int kStages = 6;
-  static constexpr int kABytes = 128 * kBK * 2;  // this CTA's 128 A rows
-  static constexpr int kBBytes = 128 * kBK * 2;  // this CTA's half of the 256-row B tile
+  static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 A rows
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of the BN-row B tile
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (200 * 1024 / kStageBytes) > 8 ? 8 : (200 * 1024 / kStageBytes);
   static constexpr int kTileBytes = kStages * kStageBytes;
   static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
   static constexpr int kTotal = 1024 + kTileBytes + kTableBytes + kMiscBytes;
 };
 
-template <int EPI, bool BF16>
+template <int BN, int EPI, bool BF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-  using L = PairLayout;
+  using L = PairLayout<BN>;
   constexpr int S = L::kStages;
-  constexpr int BN = 256;                // N of the pair tile = columns of each CTA's accumulator
+  // BN = N of the pair tile = columns of each CTA's accumulator (multiple of 32, <= 256)
+  static_assert(BN % 32 == 0 && BN <= 256 && (EPI == kEpiStore || BN % 64 == 0), "tile width");
   constexpr int kTileM = 256;
-  constexpr int kTmemCols = 2 * BN;      // two accumulators
+  constexpr int kAccStride = 256;        // TMEM columns between the two accumulators
+  constexpr int kTmemCols = 512;
   constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -110,7 +113,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int t = atomicAdd(&p.ws->tile_counter, 1);
           info.rows = 0;
           if (t < total_tiles)
-            info = decode_tile<kTileM, kOutBN, EPI>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+            info = decode_tile<kTileM, kOutBN, EPI, BN / 2>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
           if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer))
             break;
           ring[q] = info;
@@ -161,7 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!valid) break;
         if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, abort_flag, err, kDevTimeoutMma)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * kAccStride;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(&full_bar[stage], phase, abort_flag, err, kDevTimeoutMma)) {
@@ -199,7 +202,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int r_local = static_cast<int>(rank) * 128 + ew * 32 + lane;
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * kAccStride;
       OutT* out_row = reinterpret_cast<OutT*>(p.out) +
                       static_cast<size_t>(info.row0 + r_local) * p.n_out;
       store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);

@@ -205,3 +205,23 @@ def test_c_abi_direct_ctypes():
     assert code.value == 0
     # the counters are back at zero after each launch
     assert ws[:8].sum().item() == 0
+
+
+@pytest.mark.parametrize("bn", [256, 224, 192, 160, 128])
+def test_pair_tile_widths(ggo, bn, monkeypatch):
+    """Every CTA-pair tile width, forced through GGO_PAIR_BN (plain epilogue)."""
+    monkeypatch.setenv("GGO_PAIR_BN", str(bn))
+    x, w, tpe = gemm_inputs([300, 0, 17, 513, 256], 192, 1000, seed=bn)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), 3)
+    assert_parity(out, ref, f"pair bn={bn}")
+
+
+@pytest.mark.parametrize("gm", [1, 3, 8, 16])
+def test_raster_group_sizes(ggo, gm, monkeypatch):
+    monkeypatch.setenv("GGO_RASTER_GROUP_M", str(gm))
+    x, w, tpe = gemm_inputs([1100, 5, 700], 128, 640, seed=gm)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    for tc in (1, 3):
+        out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
+        assert_parity(out, ref, f"group_m={gm} tc={tc}")

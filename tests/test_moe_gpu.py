@@ -120,3 +120,13 @@ def test_fused_moe_mixtral_full_size_token_sample():
     ref = oracle.moe_layer(x[sel.to(DEV)].cpu(), logits[sel.to(DEV)].cpu(), wgu.cpu(), wd.cpu(),
                            k, round_to=torch.bfloat16)
     assert_parity(out[sel.to(DEV)], ref, "mixtral sample")
+
+
+@pytest.mark.parametrize("bn", [256, 192, 128])
+def test_swiglu_pair_tile_widths(C, bn, monkeypatch):
+    monkeypatch.setenv("GGO_PAIR_BN", str(bn))
+    # large enough that AUTO picks the CTA-pair kernel; F = 504
+    x, w, tpe = gemm_inputs([4000, 0, 6000], 128, 1008, seed=bn)
+    ref = oracle.swiglu_gemm(x, w, tpe, 3)
+    h = C.grouped_gemm_swiglu(x.to(DEV), w.to(DEV), tpe.to(DEV), 3, True)
+    assert_parity(h, ref, f"swiglu pair bn={bn}")
