@@ -270,6 +270,87 @@ def profile_run(args):
     print(f"profile {args.profile}: {args.warmup + args.steps} steps done", flush=True)
 
 
+def _skewed_counts(total, experts, skew=3.0):
+    """Power-law routing of the reference's benchmark (benchmark.py:59-69)."""
+    import torch
+    w = torch.pow(torch.arange(1, experts + 1, dtype=torch.float64), -skew)
+    w /= w.sum()
+    t = (w * total).long()
+    t[0] += total - int(t.sum())
+    return t
+
+
+def _zipf_counts(total, experts, alpha=1.2, seed=0):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    p = 1.0 / torch.arange(1, experts + 1, dtype=torch.float64) ** alpha
+    draws = torch.multinomial(p / p.sum(), total, replacement=True, generator=g)
+    return torch.bincount(draws, minlength=experts).to(torch.int64)
+
+
+def _dirichlet_counts(total, experts, alpha=0.5, seed=0):
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(seed)
+    return torch.from_numpy(rng.multinomial(total, rng.dirichlet(np.full(experts, alpha))))
+
+
+def config_sweep(steps=20, warmup=3):
+    """The other BASELINE configs at N=1 (secondary numbers; the headline is cfg2 uniform):
+    TFLOP/s of the grouped GEMM and, for the weight-bound ones, HBM GB/s of algorithmic bytes
+    (activations + weights of non-empty experts + output) over the kernel time."""
+    import torch
+    import grouped_gemm_opt as ggo
+    res = {}
+    peaks, _ = _peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    cases = [
+        ("cfg2_readme", 8, 4096, 4096, 14336, torch.tensor([512, 480, 520, 500, 510, 490, 530, 554])),
+        ("cfg2_skewed", 8, 4096, 4096, 14336, _skewed_counts(4096, 8)),
+        ("cfg3_zipf", 64, 8192, 4096, 14336, _zipf_counts(8192, 64)),
+        ("cfg3_dirichlet", 64, 8192, 4096, 14336, _dirichlet_counts(8192, 64)),
+    ]
+    for name, ex, t, k, n, tpe in cases:
+        g = torch.Generator(device="cuda").manual_seed(7)
+        x = torch.randn(t, k, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(ex, n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        td = tpe.to(torch.int64).cuda()
+        fn = lambda: ggo.grouped_gemm_opt(x, w, td)  # noqa: E731
+        for _ in range(warmup):
+            fn()
+        total, _ = _timed(fn, steps, 1)
+        ms = total / steps
+        flop = 2.0 * t * n * k
+        nz = int((tpe > 0).sum())
+        byts = t * k * 2 + nz * n * k * 2 + t * n * 2
+        res[name] = {"ms": ms, "tflops": flop / ms / 1e9, "hbm_gbs": byts / ms / 1e6,
+                     "hbm_frac": byts / ms / 1e6 / hbm, "nonzero_experts": nz,
+                     "tokens_per_expert_max": int(tpe.max())}
+        del x, w
+        torch.cuda.empty_cache()
+    # DeepSeek-V3-shaped layer on one GPU (all 256 experts local): decode and prefill token counts
+    for name, T in (("dsv3_layer_T256", 256), ("dsv3_layer_T32768", 32768)):
+        H, F, ex, k = 7168, 2048, 256, 8
+        g = torch.Generator(device="cuda").manual_seed(3)
+        x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+        logits = torch.randn(T, ex, device="cuda", generator=g)
+        wgu = (torch.randn(ex, 2 * F, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        wd = (torch.randn(ex, H, F, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        fn = lambda: ggo.fused_moe(x, logits, wgu, wd, k)  # noqa: E731
+        for _ in range(warmup):
+            fn()
+        st = max(3, steps // 4)
+        total, _ = _timed(fn, st, 1)
+        ms = total / st
+        wbytes = 3.0 * ex * F * H * 2
+        res[name] = {"ms": ms, "tokens_per_s": T / ms * 1e3,
+                     "tflops": 6.0 * T * k * H * F / ms / 1e9,
+                     "weight_gbs": wbytes / ms / 1e6, "weight_hbm_frac": wbytes / ms / 1e6 / hbm}
+        del x, wgu, wd
+        torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -278,6 +359,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the secondary-config sweep")
     ap.add_argument("--profile", choices=["gemm", "moe"], default=None,
                     help="minimal run for ncu captures: warm-up + steps of one path, no JSON")
     args = ap.parse_args()
@@ -354,6 +436,10 @@ def main():
         torch.cuda.empty_cache()
         moe = moe_layer_bench(world, rank, max(3, min(50, args.steps // 20)), 3)
 
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = config_sweep()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -381,6 +467,7 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu,
             "moe_layer": moe,
+            "configs": sweep,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

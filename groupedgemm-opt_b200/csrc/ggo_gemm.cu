@@ -126,32 +126,11 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 
-// Pair-tile width: the candidate that minimises (waves of tiles over the resident pairs) x (tile
-// width + a fixed per-tile overhead), with the m-tile count estimated from evenly split segments
-// (the counts themselves stay on the device).
-int choose_pair_bn(int64_t rows, int64_t n_out, int num_segments, bool swiglu, int pairs) {
-  static const int kPlain[] = {256, 224, 192, 160};
-  static const int kGlu[] = {256, 192, 128};
-  const int* cand = swiglu ? kGlu : kPlain;
-  const int nc = swiglu ? 3 : 4;
-  const int64_t per_seg = (rows + num_segments - 1) / num_segments;
-  int64_t mt = num_segments * ((per_seg + 255) / 256);
-  const int64_t mt_min = (rows + 255) / 256;
-  if (mt < mt_min) mt = mt_min;
-  int best = 256;
-  int64_t best_cost = INT64_MAX;
-  for (int i = 0; i < nc; ++i) {
-    const int out = swiglu ? cand[i] / 2 : cand[i];
-    const int64_t tiles = mt * ((n_out + out - 1) / out);
-    const int64_t waves = (tiles + pairs - 1) / pairs;
-    const int64_t cost = waves * (cand[i] + 16);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = cand[i];
-    }
-  }
-  return best;
-}
+// Pair-tile width. 256 is the default: measured on cfg2 under the 1 kW power cap, 256-wide tiles
+// beat 224-wide ones per SM clock (0.87 vs 0.81 TFLOP/s per MHz) although the 224-wide grid has a
+// fuller last wave; wider tiles move fewer operand bytes per FLOP, and energy per FLOP sets the
+// clock the GPU can hold. GGO_PAIR_BN selects another width for experiments.
+constexpr int kDefaultPairBN = 256;
 
 template <int EPI, bool BF16>
 int launch_pair_bn(int bn, const void* a, const void* b, int64_t b_rows, const GemmParams& p,
@@ -250,8 +229,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
   if (bn == 512) {
-    const int pbn = env_int("GGO_PAIR_BN",
-                            choose_pair_bn(rows, n, num_segments, swiglu, g_sm_count[dev] / 2));
+    const int pbn = env_int("GGO_PAIR_BN", kDefaultPairBN);
     if (swiglu)
       return bf16 ? launch_pair_bn<kEpiSwiGLU, true>(pbn, input, weights, b_rows, p, dev, stream)
                   : launch_pair_bn<kEpiSwiGLU, false>(pbn, input, weights, b_rows, p, dev, stream);
