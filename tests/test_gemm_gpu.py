@@ -225,3 +225,14 @@ def test_raster_group_sizes(ggo, gm, monkeypatch):
     for tc in (1, 3):
         out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
         assert_parity(out, ref, f"group_m={gm} tc={tc}")
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_host_buffer_api(ggo, chunks):
+    """grouped_gemm_opt_host: pinned host activations/output, overlapped per expert chunk."""
+    x, w, tpe = gemm_inputs([300, 0, 17, 513, 256, 0, 90, 1], 256, 384, seed=chunks)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt_host(x.pin_memory(), w.to(DEV), tpe, chunks=chunks)
+    torch.cuda.synchronize()
+    assert not out.is_cuda
+    assert_parity(out, ref, f"host api chunks={chunks}")
