@@ -408,6 +408,26 @@ def main():
                                                               FALLBACK_PEAKS["bf16_tflops"])))
     ggo.check_device_errors(local)
 
+    # The reference's headline (README.md:4-5, benchmark.py:86-88, 338-347): grouped-GEMM latency
+    # vs one dense cuBLAS GEMM of equal FLOPs, [T,K] x [K,N], timed the same way on this GPU.
+    xd_dense = x
+    wd_dense = w[0].contiguous()  # [N, K]
+    dense_fn = lambda: torch.nn.functional.linear(xd_dense, wd_dense)  # noqa: E731
+    for _ in range(args.warmup):
+        dense_fn()
+    with ClockSampler(local) as clk_d:
+        t_end = time.time() + 1.0
+        while time.time() < t_end:
+            for _ in range(50):
+                dense_fn()
+            torch.cuda.synchronize()
+        dense_total, _ = _timed(dense_fn, args.steps, world)
+    dense_ms = dense_total / args.steps
+    vs_dense = {"dense_cublas_tflops": FLOP_PER_STEP / dense_ms / 1e9,
+                "dense_ms": dense_ms, "grouped_ms": ms, "efficiency": dense_ms / ms,
+                "dense_clocks": clk_d.summary(),
+                "what": "F.linear [4096,4096]x[14336,4096]^T (cuBLAS), same FLOPs as one step"}
+
     # e2e through the public API with host buffers: H2D of the step's activations and counts
     # from pinned memory, the call, D2H of the full output into pinned memory.
     x_h = x.cpu().pin_memory()
@@ -474,6 +494,7 @@ def main():
             "gpu_launches": args.steps,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "vs_dense_gemm": vs_dense,
             "moe_layer": moe,
             "configs": sweep,
         }
