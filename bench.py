@@ -309,6 +309,7 @@ def config_sweep(steps=20, warmup=3):
         ("cfg2_skewed", 8, 4096, 4096, 14336, _skewed_counts(4096, 8)),
         ("cfg3_zipf", 64, 8192, 4096, 14336, _zipf_counts(8192, 64)),
         ("cfg3_dirichlet", 64, 8192, 4096, 14336, _dirichlet_counts(8192, 64)),
+        ("single_expert_8192cubed", 1, 8192, 8192, 8192, torch.tensor([8192])),
     ]
     for name, ex, t, k, n, tpe in cases:
         g = torch.Generator(device="cuda").manual_seed(7)
