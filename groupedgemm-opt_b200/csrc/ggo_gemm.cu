@@ -6,6 +6,7 @@
 // cudaStreamSynchronize), zero-token experts are skipped inside the kernel, and there is no
 // per-group argument buffer to build or copy.
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 
@@ -195,17 +196,35 @@ int choose_bn(int tile_config, int64_t rows, int64_t n, int num_segments, int sm
   }
 }
 
+// Expert-parallel extensions of one call (see ggo_ep_grouped_gemm).
+struct GemmExtras {
+  int rows_is_bound;
+  const int32_t* origin;
+  void* const* peer_out;
+  int world;
+};
+
 int gemm_common(const void* input, const void* weights, void* output, const int64_t* counts,
                 int num_segments, int num_experts, int64_t rows, int64_t n, int64_t k, int dtype,
-                int tile_config, int sort_by_m, void* workspace, cudaStream_t stream, bool swiglu) {
-  if (!input || !weights || !output || !counts || !workspace) return GGO_ERR_INVALID_ARG;
+                int tile_config, int sort_by_m, void* workspace, cudaStream_t stream, bool swiglu,
+                const GemmExtras* ex = nullptr) {
+  const bool scatter = ex && ex->origin;
+  if (!input || !weights || (!output && !scatter) || !counts || !workspace)
+    return GGO_ERR_INVALID_ARG;
+  if (scatter) {
+    if (ex->world < 1 || ex->world > 8 || num_segments % num_experts ||
+        num_segments / num_experts > ex->world)
+      return GGO_ERR_INVALID_ARG;
+    for (int r = 0; r < ex->world; ++r)
+      if (!ex->peer_out[r] || !aligned16(ex->peer_out[r])) return GGO_ERR_ALIGNMENT;
+  }
   if (num_segments <= 0 || num_experts <= 0 || rows < 0 || n <= 0 || k <= 0)
     return GGO_ERR_INVALID_ARG;
   if (tile_config < 0 || tile_config > GGO_TILE_CUBLAS_SEQ) return GGO_ERR_INVALID_ARG;
   if (num_segments > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
   if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
   if ((k % 8) || (n % 8)) return GGO_ERR_ALIGNMENT;
-  if (!aligned16(input) || !aligned16(weights) || !aligned16(output) ||
+  if (!aligned16(input) || !aligned16(weights) || (output && !aligned16(output)) ||
       (reinterpret_cast<uintptr_t>(workspace) & 3u))
     return GGO_ERR_ALIGNMENT;
   const int64_t b_rows = static_cast<int64_t>(num_experts) * (swiglu ? 2 * n : n);
@@ -224,6 +243,9 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.k = static_cast<int>(k);
   p.sort_by_m = sort_by_m ? 1 : 0;
   p.group_m = raster_group_m();
+  p.rows_is_bound = ex ? ex->rows_is_bound : 0;
+  p.origin = scatter ? ex->origin : nullptr;
+  for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;
   p.out = output;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
@@ -338,6 +360,52 @@ int ggo_grouped_gemm_noalloc(const void* input_dev, const void* weights_dev, voi
                           num_experts, total_tokens, N, K, dtype, tile_config, sort_by_m, scratch,
                           stream, false);
 }
+
+int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,
+                        const int64_t* tokens_per_segment_dev, int num_segments, int num_experts,
+                        int64_t capacity_rows, int64_t N, int64_t K, int dtype, int swiglu,
+                        const int32_t* origin_dev, void* const* peer_out, int world_size,
+                        int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  ggo::GemmExtras ex;
+  ex.rows_is_bound = 1;
+  ex.origin = origin_dev;
+  ex.peer_out = peer_out;
+  ex.world = world_size;
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_segment_dev,
+                          num_segments, num_experts, capacity_rows, N, K, dtype, GGO_TILE_AUTO,
+                          sort_by_m, workspace_dev, stream, swiglu != 0, &ex);
+}
+
+int ggo_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out) {
+  if (!ptr_out || !handle_out || bytes == 0) return GGO_ERR_INVALID_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return GGO_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return GGO_ERR_CUDA;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr_out = p;
+  return GGO_OK;
+}
+
+int ggo_ipc_open(const void* handle, void** ptr_out) {
+  if (!handle || !ptr_out) return GGO_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return GGO_ERR_CUDA;
+  *ptr_out = p;
+  return GGO_OK;
+}
+
+int ggo_ipc_close(void* peer_ptr) {
+  return cudaIpcCloseMemHandle(peer_ptr) == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+}
+
+int ggo_ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? GGO_OK : GGO_ERR_CUDA; }
 
 int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out) {
   if (!workspace_dev || !status_out) return GGO_ERR_INVALID_ARG;

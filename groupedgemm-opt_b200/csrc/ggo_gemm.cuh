@@ -70,6 +70,11 @@ struct GemmParams {
   int sort_by_m;          // process segments heaviest-first
   int group_m;            // m-tiles per raster group (>= 1)
   void* out;              // [rows, n_out], bf16 or fp16
+  int rows_is_bound;      // 1: `rows` is a capacity; counts may sum to less (no mismatch error)
+  // Scatter epilogue (expert parallelism): when `origin` is set, output row r goes to
+  // peer_out[segment / num_experts] + origin[r] * n_out instead of out + r * n_out.
+  const int32_t* origin;
+  void* peer_out[8];
   GgoWorkspace* ws;
 };
 
@@ -79,7 +84,8 @@ struct TileInfo {
   int n0;      // first output column
   int brow0;   // first W row of box 0 (and box 1 = brow1)
   int brow1;
-  int pad[3];
+  int seg;     // segment of the tile
+  int pad[2];
 };
 
 template <int BN>
@@ -129,7 +135,8 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
       if (s < nseg) t_rowoff[s] = carry + x - v;
       carry += __shfl_sync(0xffffffffu, x, 31);
     }
-    if (lane == 0 && carry != p.rows && blockIdx.x == 0) atomicCAS(err, 0, kDevCountMismatch);
+    const bool bad = p.rows_is_bound ? carry > p.rows : carry != p.rows;
+    if (lane == 0 && bad && blockIdx.x == 0) atomicCAS(err, 0, kDevCountMismatch);
   }
   // Processing order: identity, or heaviest segment first (ties by index) via a bitonic sort of
   // 64-bit keys held temporarily in the (still unused) operand tile buffers.
@@ -215,6 +222,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
   TileInfo info;
   info.row0 = t_rowoff[seg] + m_idx * TILE_M;
   info.rows = min(TILE_M, t_cnt[seg] - m_idx * TILE_M);
+  info.seg = seg;
   info.n0 = n_idx * OUT_BN;
   if (EPI == kEpiSwiGLU) {
     info.brow0 = expert * p.n_b + info.n0;                 // gate rows
@@ -299,6 +307,18 @@ __device__ __forceinline__ void store_tile_row(uint32_t t_row, int n0, int n_out
       }
     }
   }
+}
+
+// Destination of accumulator row r_local of a tile: the local output row, or (scatter epilogue)
+// the row on the source rank given by `origin`, through that rank's peer mapping.
+template <typename OutT>
+__device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo& info, int r_local,
+                                            bool row_ok) {
+  const int r = info.row0 + r_local;
+  if (p.origin == nullptr || !row_ok)
+    return reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(r) * p.n_out;
+  const int src = info.seg / p.num_experts;
+  return reinterpret_cast<OutT*>(p.peer_out[src]) + static_cast<size_t>(p.origin[r]) * p.n_out;
 }
 
 template <int BN, int EPI, bool BF16>
@@ -452,8 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      OutT* out_row = reinterpret_cast<OutT*>(p.out) +
-                      static_cast<size_t>(info.row0 + r_local) * p.n_out;
+      OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
       tc_fence_before();
       __syncwarp();
@@ -463,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ------------------------------------------------------------------ tear-down
+  if (p.origin) __threadfence_system();  // scattered rows visible to the peers before exit
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();

@@ -119,7 +119,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ring[q] = info;
           const uint32_t pr = mapa_shared(&ring[q], 1);
           st_cluster_v4(pr, info.row0, info.rows, info.n0, info.brow0);
-          st_cluster_v4(pr + 16, info.brow1, 0, 0, 0);
+          st_cluster_v4(pr + 16, info.brow1, info.seg, 0, 0);
           mbar_arrive(&schf_bar[q]);
           mbar_arrive_cluster(mapa_shared(&schf_bar[q], 1));
         } else {
@@ -203,8 +203,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int r_local = static_cast<int>(rank) * 128 + ew * 32 + lane;
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * kAccStride;
-      OutT* out_row = reinterpret_cast<OutT*>(p.out) +
-                      static_cast<size_t>(info.row0 + r_local) * p.n_out;
+      OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
       tc_fence_before();
       __syncwarp();
@@ -214,6 +213,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 
   // ------------------------------------------------------------------ tear-down
+  if (p.origin) __threadfence_system();  // scattered rows visible to the peers before exit
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no remote arrive or ring store may target a CTA that has exited

@@ -17,7 +17,8 @@
 namespace ggo {
 namespace {
 
-constexpr int kRouteTokens = 128;  // tokens per route/permute block
+constexpr int kRouteTokens = 32;   // tokens per route/dispatch block
+constexpr int kMaxPeers = 8;       // expert-parallel ranks a dispatch can address
 constexpr int kRouteThreads = 256;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopK = 16;
@@ -95,11 +96,13 @@ __global__ void __launch_bounds__(kRouteThreads)
     block_counts[static_cast<size_t>(blockIdx.x) * E + e] = static_cast<int>(hist[e]);
 }
 
-// One block of 1024 threads. Turns block_counts[b][e] into absolute start rows (in place) and
-// writes tokens_per_expert.
+// One block of 1024 threads. Turns block_counts[b][e] into absolute start rows (in place),
+// writes tokens_per_expert and the exclusive start row of every expert (expert_start[E], stored
+// right after the nblocks x E table).
 __global__ void __launch_bounds__(1024)
     route_scan_kernel(int* __restrict__ block_counts, int nblocks, int E,
                       int64_t* __restrict__ tpe) {
+  int* expert_start = block_counts + static_cast<size_t>(nblocks) * E;
   __shared__ int tot[kMaxExperts];
   const int e = threadIdx.x;
   int sum = 0;
@@ -116,6 +119,7 @@ __global__ void __launch_bounds__(1024)
   if (e < E) {
     int run = tot[e] - sum;  // exclusive start of expert e
     tpe[e] = sum;
+    expert_start[e] = run;
     for (int b = 0; b < nblocks; ++b) {
       const size_t i = static_cast<size_t>(b) * E + e;
       const int c = block_counts[i];
@@ -125,22 +129,55 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// grid = ceil(T / kRouteTokens). Positions by one warp, row gather by all warps.
+// Where dispatched rows go. world == 1: recv[0] is the local expert-sorted buffer and a row's
+// destination is its sorted position. world > 1 (expert parallelism): rank r owns experts
+// [r*el, (r+1)*el); recv[r] is rank r's receive buffer (a peer mapping for r != rank) laid out as
+// [source rank][local expert] segments whose sizes come from counts_all [world][E]
+// (every rank's tokens_per_expert), and origin[r][dst] receives the row's sorted position on
+// the source rank (where its result must come back).
+template <typename T16>
+struct DispatchTargets {
+  int world;
+  int rank;
+  int el;
+  const int64_t* counts_all;
+  T16* recv[kMaxPeers];
+  int32_t* origin[kMaxPeers];
+};
+
+// grid = ceil(T / kRouteTokens). Sorted positions by one warp (deterministic in-block ranks),
+// destination rows from per-expert bases, then the row copy by all warps (each token's row read
+// once, written top_k times, four 16-byte chunks in flight per lane).
 template <typename T16>
 __global__ void __launch_bounds__(kRouteThreads)
-    permute_kernel(const T16* __restrict__ x, int T, int H, int E, int K,
-                   const int32_t* __restrict__ topk_ids, const int* __restrict__ block_offsets,
-                   T16* __restrict__ xs, int32_t* __restrict__ sorted_token,
-                   int32_t* __restrict__ slot_pos) {
+    dispatch_kernel(const T16* __restrict__ x, int T, int H, int E, int K,
+                    const int32_t* __restrict__ topk_ids, const int* __restrict__ block_offsets,
+                    const int* __restrict__ expert_start, const DispatchTargets<T16> tg,
+                    int32_t* __restrict__ sorted_token, int32_t* __restrict__ slot_pos) {
   extern __shared__ int psm[];
-  int* off = psm;        // [E]
-  int* pos = psm + E;    // [kRouteTokens * K]
+  int* off = psm;             // [E] running sorted position per expert (this block)
+  int* dbase = psm + E;       // [E] destination row of the expert's first row from this rank
+  int* pos = dbase + E;       // [kRouteTokens * K] sorted position per entry
+  int* drow = pos + kRouteTokens * K;  // [kRouteTokens * K] destination row per entry
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kRouteTokens;
   const int ntok = min(kRouteTokens, T - t0);
   const int nent = ntok * K;
-  for (int e = threadIdx.x; e < E; e += kRouteThreads)
+  for (int e = threadIdx.x; e < E; e += kRouteThreads) {
     off[e] = block_offsets[static_cast<size_t>(blockIdx.x) * E + e];
+    if (tg.world == 1) {
+      dbase[e] = expert_start[e];
+    } else {
+      // rows from lower source ranks for the owner's experts, then this rank's rows for the
+      // owner's lower local experts
+      const int r = e / tg.el, le = e % tg.el;
+      long long b = 0;
+      for (int s = 0; s < tg.rank; ++s)
+        for (int j = 0; j < tg.el; ++j) b += tg.counts_all[static_cast<size_t>(s) * E + r * tg.el + j];
+      for (int j = 0; j < le; ++j) b += tg.counts_all[static_cast<size_t>(tg.rank) * E + r * tg.el + j];
+      dbase[e] = static_cast<int>(b);
+    }
+  }
   __syncthreads();
   if (warp == 0) {
     const int32_t* ids = topk_ids + static_cast<size_t>(t0) * K;
@@ -151,15 +188,17 @@ __global__ void __launch_bounds__(kRouteThreads)
       if (valid) {
         const int id = ids[i];
         const unsigned peers = __match_any_sync(vmask, id);
-        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const int rank_in = __popc(peers & ((1u << lane) - 1u));
         const int b = off[id];
         __syncwarp(vmask);
         if (lane == __ffs(peers) - 1) off[id] = b + __popc(peers);
-        const int ps = b + rank;
+        const int ps = b + rank_in;
         pos[i] = ps;
-        const int t = t0 + i / K;
+        const int d = dbase[id] + (ps - expert_start[id]);
+        drow[i] = d;
         slot_pos[static_cast<size_t>(t0) * K + i] = ps;
-        sorted_token[ps] = t;
+        if (sorted_token) sorted_token[ps] = t0 + i / K;
+        if (tg.world > 1) tg.origin[id / tg.el][d] = ps;
       }
       __syncwarp();
     }
@@ -168,14 +207,26 @@ __global__ void __launch_bounds__(kRouteThreads)
   const int vec = H / 8;  // 16-byte chunks per row
   for (int tl = warp; tl < ntok; tl += kRouteThreads / 32) {
     const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t0 + tl) * H);
-    for (int c = lane; c < vec; c += 32) {
-      const uint4 v = src[c];
+    for (int c0 = lane; c0 < vec; c0 += 32 * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        if (c < vec) v[u] = src[c];
+      }
       for (int j = 0; j < K; ++j) {
-        uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<size_t>(pos[tl * K + j]) * H);
-        dst[c] = v;
+        const int e = tl * K + j;
+        const int r = tg.world > 1 ? topk_ids[static_cast<size_t>(t0) * K + e] / tg.el : 0;
+        uint4* dst = reinterpret_cast<uint4*>(tg.recv[r] + static_cast<size_t>(drow[e]) * H);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + 32 * u;
+          if (c < vec) dst[c] = v[u];
+        }
       }
     }
   }
+  if (tg.world > 1) __threadfence_system();
 }
 
 template <typename T16>
@@ -223,6 +274,52 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int nblocks_for(int64_t T) { return static_cast<int>((T + kRouteTokens - 1) / kRouteTokens); }
 
+template <typename T16>
+void launch_dispatch(const void* x, int T, int H, int E, int K, const int32_t* ids,
+                     const int* bo, const int* es, const int64_t* counts_all, int world, int rank,
+                     void* const* recv, int32_t* const* origin, int32_t* stok, int32_t* spos,
+                     cudaStream_t stream) {
+  DispatchTargets<T16> tg;
+  tg.world = world;
+  tg.rank = rank;
+  tg.el = E / world;
+  tg.counts_all = counts_all;
+  for (int r = 0; r < kMaxPeers; ++r) {
+    tg.recv[r] = r < world ? static_cast<T16*>(recv[r]) : nullptr;
+    tg.origin[r] = r < world ? origin[r] : nullptr;
+  }
+  const int nb = nblocks_for(T);
+  const size_t smem = (2 * static_cast<size_t>(E) + 2 * kRouteTokens * K) * 4;
+  dispatch_kernel<T16><<<nb, kRouteThreads, smem, stream>>>(
+      static_cast<const T16*>(x), T, H, E, K, ids, bo, es, tg, stok, spos);
+}
+
+int dispatch_common(const void* x, int64_t num_tokens, int64_t hidden, int E, int K,
+                    const int32_t* ids, const void* scratch, const int64_t* counts_all, int world,
+                    int rank, void* const* recv, int32_t* const* origin, int32_t* stok,
+                    int32_t* spos, int dtype, cudaStream_t stream) {
+  if (!x || !ids || !spos || !scratch) return GGO_ERR_INVALID_ARG;
+  if (num_tokens < 0 || hidden <= 0 || E <= 0 || E > kMaxExperts || K <= 0 || K > kMaxTopK)
+    return GGO_ERR_INVALID_ARG;
+  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
+  if (hidden % 8 || !aligned16(x)) return GGO_ERR_ALIGNMENT;
+  for (int r = 0; r < world; ++r)
+    if (!aligned16(recv[r])) return GGO_ERR_ALIGNMENT;
+  if (num_tokens * K > INT32_MAX || hidden > INT32_MAX) return GGO_ERR_SHAPE;
+  const int T = static_cast<int>(num_tokens);
+  const int nb = nblocks_for(T);
+  if (nb == 0) return GGO_OK;
+  const int* bo = static_cast<const int*>(scratch);
+  const int* es = bo + static_cast<size_t>(nb) * E;
+  if (dtype == GGO_DTYPE_BF16)
+    launch_dispatch<__nv_bfloat16>(x, T, static_cast<int>(hidden), E, K, ids, bo, es, counts_all,
+                                   world, rank, recv, origin, stok, spos, stream);
+  else
+    launch_dispatch<__half>(x, T, static_cast<int>(hidden), E, K, ids, bo, es, counts_all, world,
+                            rank, recv, origin, stok, spos, stream);
+  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+}
+
 }  // namespace
 }  // namespace ggo
 
@@ -230,7 +327,7 @@ extern "C" {
 
 size_t ggo_moe_route_scratch_bytes(int64_t num_tokens, int num_experts) {
   if (num_tokens <= 0 || num_experts <= 0) return 16;
-  return static_cast<size_t>(ggo::nblocks_for(num_tokens)) * num_experts * sizeof(int);
+  return (static_cast<size_t>(ggo::nblocks_for(num_tokens)) + 1) * num_experts * sizeof(int);
 }
 
 int ggo_moe_route(const float* logits_dev, int64_t num_tokens, int num_experts, int top_k,
@@ -262,32 +359,27 @@ int ggo_moe_permute(const void* x_dev, int64_t num_tokens, int64_t hidden, int n
                     int top_k, const int32_t* topk_ids_dev, void* x_sorted_dev,
                     int32_t* sorted_token_dev, int32_t* slot_pos_dev, void* scratch_dev,
                     int dtype, cudaStream_t stream) {
-  if (!x_dev || !topk_ids_dev || !x_sorted_dev || !sorted_token_dev || !slot_pos_dev ||
-      !scratch_dev)
+  if (!x_sorted_dev || !sorted_token_dev) return GGO_ERR_INVALID_ARG;
+  void* recv[1] = {x_sorted_dev};
+  int32_t* origin[1] = {nullptr};
+  return ggo::dispatch_common(x_dev, num_tokens, hidden, num_experts, top_k, topk_ids_dev,
+                              scratch_dev, nullptr, 1, 0, recv, origin, sorted_token_dev,
+                              slot_pos_dev, dtype, stream);
+}
+
+int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int num_experts,
+                    int top_k, const int32_t* topk_ids_dev, const void* scratch_dev,
+                    const int64_t* counts_all_dev, int world_size, int rank,
+                    void* const* recv_rows, int32_t* const* recv_origin, int32_t* slot_pos_dev,
+                    int dtype, cudaStream_t stream) {
+  if (world_size < 1 || world_size > ggo::kMaxPeers || rank < 0 || rank >= world_size ||
+      !counts_all_dev || !recv_rows || !recv_origin || num_experts % world_size)
     return GGO_ERR_INVALID_ARG;
-  if (num_tokens < 0 || hidden <= 0 || num_experts <= 0 || num_experts > ggo::kMaxExperts ||
-      top_k <= 0 || top_k > ggo::kMaxTopK)
-    return GGO_ERR_INVALID_ARG;
-  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
-  if (hidden % 8 || !ggo::aligned16(x_dev) || !ggo::aligned16(x_sorted_dev))
-    return GGO_ERR_ALIGNMENT;
-  if (num_tokens * top_k > INT32_MAX || hidden > INT32_MAX) return GGO_ERR_SHAPE;
-  const int T = static_cast<int>(num_tokens);
-  const int nb = ggo::nblocks_for(T);
-  if (nb == 0) return GGO_OK;
-  const size_t smem = (static_cast<size_t>(num_experts) + ggo::kRouteTokens * top_k) * 4;
-  const int* bo = static_cast<const int*>(scratch_dev);
-  if (dtype == GGO_DTYPE_BF16) {
-    ggo::permute_kernel<__nv_bfloat16><<<nb, ggo::kRouteThreads, smem, stream>>>(
-        static_cast<const __nv_bfloat16*>(x_dev), T, static_cast<int>(hidden), num_experts, top_k,
-        topk_ids_dev, bo, static_cast<__nv_bfloat16*>(x_sorted_dev), sorted_token_dev,
-        slot_pos_dev);
-  } else {
-    ggo::permute_kernel<__half><<<nb, ggo::kRouteThreads, smem, stream>>>(
-        static_cast<const __half*>(x_dev), T, static_cast<int>(hidden), num_experts, top_k,
-        topk_ids_dev, bo, static_cast<__half*>(x_sorted_dev), sorted_token_dev, slot_pos_dev);
-  }
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  for (int r = 0; r < world_size; ++r)
+    if (!recv_rows[r] || !recv_origin[r]) return GGO_ERR_INVALID_ARG;
+  return ggo::dispatch_common(x_dev, num_tokens, hidden, num_experts, top_k, topk_ids_dev,
+                              scratch_dev, counts_all_dev, world_size, rank, recv_rows,
+                              recv_origin, nullptr, slot_pos_dev, dtype, stream);
 }
 
 int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,

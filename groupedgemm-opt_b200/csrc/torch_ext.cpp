@@ -11,7 +11,9 @@
 
 #include <map>
 #include <mutex>
+#include <string>
 #include <tuple>
+#include <vector>
 
 #include "ggo.h"
 
@@ -191,6 +193,100 @@ int64_t workspace_error(int64_t device) {
   return code;
 }
 
+// ------------------------------------------------------------------ expert parallelism (IPC)
+// Allocates `nbytes` of device memory shareable with the other processes of the node; returns
+// (address, 64-byte handle).
+std::tuple<int64_t, py::bytes> ipc_alloc(int64_t nbytes) {
+  void* p = nullptr;
+  char h[GGO_IPC_HANDLE_BYTES];
+  check_status(ggo_ipc_alloc(static_cast<size_t>(nbytes), &p, h), "IPC alloc");
+  return {reinterpret_cast<int64_t>(p), py::bytes(h, GGO_IPC_HANDLE_BYTES)};
+}
+
+int64_t ipc_open(py::bytes handle) {
+  std::string h = handle;
+  TORCH_CHECK(h.size() == GGO_IPC_HANDLE_BYTES, "bad IPC handle size");
+  void* p = nullptr;
+  check_status(ggo_ipc_open(h.data(), &p), "IPC open");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { check_status(ggo_ipc_close(reinterpret_cast<void*>(ptr)), "IPC close"); }
+void ipc_free(int64_t ptr) { check_status(ggo_ipc_free(reinterpret_cast<void*>(ptr)), "IPC free"); }
+
+// Non-owning tensor view of device memory at `ptr` (the caller keeps the memory alive).
+torch::Tensor tensor_view(int64_t ptr, std::vector<int64_t> shape, torch::Dtype dtype,
+                          int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA,
+                                                        static_cast<c10::DeviceIndex>(device));
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
+}
+
+// Expert-parallel dispatch; returns slot_pos [T*k] int32.
+torch::Tensor ep_dispatch(const torch::Tensor& x, const torch::Tensor& topk_ids,
+                          const torch::Tensor& scratch, const torch::Tensor& counts_all,
+                          int64_t rank, std::vector<int64_t> recv_ptrs,
+                          std::vector<int64_t> origin_ptrs) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "hidden must be 2D contiguous CUDA");
+  TORCH_CHECK(counts_all.scalar_type() == torch::kInt64 && counts_all.dim() == 2 &&
+                  counts_all.is_contiguous(), "counts_all must be contiguous int64 [world, E]");
+  const int world = static_cast<int>(recv_ptrs.size());
+  TORCH_CHECK(world == static_cast<int>(origin_ptrs.size()) && world == counts_all.size(0) &&
+                  world <= GGO_MAX_EP_RANKS, "one receive buffer and origin buffer per rank");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x.size(0), H = x.size(1), k = topk_ids.size(1);
+  auto spos = torch::empty({T * k}, torch::TensorOptions().dtype(torch::kInt32).device(x.device()));
+  std::vector<void*> recv(world);
+  std::vector<int32_t*> orig(world);
+  for (int r = 0; r < world; ++r) {
+    recv[r] = reinterpret_cast<void*>(recv_ptrs[r]);
+    orig[r] = reinterpret_cast<int32_t*>(origin_ptrs[r]);
+  }
+  const int st = ggo_ep_dispatch(x.data_ptr(), T, H, static_cast<int>(counts_all.size(1)),
+                                 static_cast<int>(k), topk_ids.data_ptr<int32_t>(),
+                                 scratch.data_ptr(), counts_all.data_ptr<int64_t>(), world,
+                                 static_cast<int>(rank), recv.data(), orig.data(),
+                                 spos.data_ptr<int32_t>(), dtype_code(x), stream);
+  check_status(st, "expert-parallel dispatch");
+  return spos;
+}
+
+// Grouped GEMM over a capacity-sized receive buffer. Returns the output [capacity, N] unless the
+// scatter epilogue is used (origin given), in which case results go to peer_out and an empty
+// tensor is returned.
+torch::Tensor ep_grouped_gemm(const torch::Tensor& input, const torch::Tensor& weights,
+                              const torch::Tensor& seg_counts, int64_t num_experts, bool swiglu,
+                              c10::optional<torch::Tensor> origin,
+                              std::vector<int64_t> peer_out, bool sort_by_m) {
+  check_operands(input, weights);
+  c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t cap = input.size(0), K = input.size(1);
+  const int64_t N = swiglu ? weights.size(1) / 2 : weights.size(1);
+  torch::Tensor out;
+  const int32_t* org = nullptr;
+  std::vector<void*> peers(peer_out.size());
+  for (size_t r = 0; r < peer_out.size(); ++r) peers[r] = reinterpret_cast<void*>(peer_out[r]);
+  if (origin.has_value()) {
+    TORCH_CHECK(origin->scalar_type() == torch::kInt32 && origin->numel() >= cap,
+                "origin must be int32 with one entry per row");
+    org = origin->data_ptr<int32_t>();
+    out = torch::empty({0, N}, input.options());
+  } else {
+    out = torch::empty({cap, N}, input.options());
+  }
+  if (cap == 0) return out;
+  auto c = counts_on_device(seg_counts, input.device());
+  const int st = ggo_ep_grouped_gemm(
+      input.data_ptr(), weights.data_ptr(), org ? nullptr : out.data_ptr(),
+      c.data_ptr<int64_t>(), static_cast<int>(c.size(0)), static_cast<int>(num_experts), cap, N,
+      K, dtype_code(input), swiglu ? 1 : 0, org, peers.data(), static_cast<int>(peers.size()),
+      sort_by_m ? 1 : 0, workspace_for(input.device(), stream), stream);
+  check_status(st, "expert-parallel grouped GEMM");
+  return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -210,4 +306,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("slot_pos"));
   m.def("workspace_error", &workspace_error, py::arg("device") = 0);
   m.def("abi_version", []() { return ggo_version(); });
+  m.def("ipc_alloc", &ipc_alloc, py::arg("nbytes"));
+  m.def("ipc_open", &ipc_open, py::arg("handle"));
+  m.def("ipc_close", &ipc_close, py::arg("ptr"));
+  m.def("ipc_free", &ipc_free, py::arg("ptr"));
+  m.def("tensor_view", &tensor_view, py::arg("ptr"), py::arg("shape"), py::arg("dtype"),
+        py::arg("device"));
+  m.def("ep_dispatch", &ep_dispatch, py::arg("hidden"), py::arg("topk_ids"), py::arg("scratch"),
+        py::arg("counts_all"), py::arg("rank"), py::arg("recv_ptrs"), py::arg("origin_ptrs"));
+  m.def("ep_grouped_gemm", &ep_grouped_gemm, py::arg("input"), py::arg("weights"),
+        py::arg("seg_counts"), py::arg("num_experts"), py::arg("swiglu"), py::arg("origin"),
+        py::arg("peer_out"), py::arg("sort_by_m") = true);
 }

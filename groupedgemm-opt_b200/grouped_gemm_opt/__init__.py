@@ -6,7 +6,7 @@ from grouped_gemm_opt.ops import (TileConfig, check_device_errors, grouped_gemm_
                                   grouped_gemm_opt_host)
 from grouped_gemm_opt.triton_fused_moe import triton_fused_moe
 from grouped_gemm_opt.triton_grouped_gemm import triton_grouped_gemm
-from grouped_gemm_opt.moe import fused_moe
+from grouped_gemm_opt.moe import EPBuffers, fused_moe
 
 __all__ = ["grouped_gemm_opt", "TileConfig", "triton_fused_moe", "triton_grouped_gemm",
-           "fused_moe", "check_device_errors", "grouped_gemm_opt_host"]
+           "fused_moe", "check_device_errors", "grouped_gemm_opt_host", "EPBuffers"]

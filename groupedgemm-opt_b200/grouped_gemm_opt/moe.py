@@ -57,6 +57,104 @@ def cuda_ops() -> MoEOps:
     )
 
 
+class EPBuffers:
+    """Receive buffers of the fused expert-parallel path, shared between the ranks of one node
+    through CUDA IPC. Create once per (group, sizes) on every rank (a collective call):
+
+        bufs = EPBuffers(group, max_tokens_per_rank, hidden, top_k, num_experts, torch.bfloat16)
+        out = fused_moe(x, logits, w_gu_local, w_d_local, top_k, ep_group=group, ep_buffers=bufs)
+
+    Per rank: recv rows [capacity, H] and their origins [capacity] int32, where capacity =
+    world * max_tokens * top_k (every routed row of every rank fits even if all go to one rank),
+    and the return buffer [max_tokens * top_k, H] that owners scatter results into.
+    """
+
+    def __init__(self, group, max_tokens: int, hidden: int, top_k: int, num_experts: int,
+                 dtype=torch.bfloat16, device=None):
+        from grouped_gemm_opt._native import _C
+        self._C = _C
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        assert self.world <= 8, "the fused path addresses at most 8 ranks (one NVLink domain)"
+        assert num_experts % self.world == 0
+        self.max_tokens, self.hidden, self.top_k = max_tokens, hidden, top_k
+        self.num_experts, self.dtype = num_experts, dtype
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.capacity = self.world * max_tokens * top_k
+        esz = torch.empty(0, dtype=dtype).element_size()
+        sizes = {"recv": self.capacity * hidden * esz, "origin": self.capacity * 4,
+                 "back": max_tokens * top_k * hidden * esz}
+        self._own = {}
+        handles = {}
+        for name, nbytes in sizes.items():
+            ptr, h = _C.ipc_alloc(max(nbytes, 256))
+            self._own[name] = ptr
+            handles[name] = h
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=group)
+        self.ptrs = {name: [] for name in sizes}
+        self._opened = []
+        for r in range(self.world):
+            for name in sizes:
+                if r == self.rank:
+                    self.ptrs[name].append(self._own[name])
+                else:
+                    ptr = _C.ipc_open(gathered[r][name])
+                    self._opened.append(ptr)
+                    self.ptrs[name].append(ptr)
+        dev = self.device.index
+        self.recv = _C.tensor_view(self._own["recv"], [self.capacity, hidden], dtype, dev)
+        self.origin = _C.tensor_view(self._own["origin"], [self.capacity], torch.int32, dev)
+        self.back = _C.tensor_view(self._own["back"], [max_tokens * top_k, hidden], dtype, dev)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        dist.barrier(group=group)
+
+    def fence(self):
+        """Stream-ordered cross-rank barrier: a one-element all-reduce. Every rank's earlier
+        kernels (and their peer stores) are complete when it returns on any rank's stream."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self):
+        if self._C is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            self._C.ipc_close(p)
+        dist.barrier(group=self.group)
+        for p in self._own.values():
+            self._C.ipc_free(p)
+        self._C = None
+
+
+def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuffers",
+                   sort_by_m):
+    """Expert-parallel layer over NVLink peer memory: the dispatch kernel writes rows into the
+    owners' receive buffers, the down GEMM's epilogue writes results back into the sources'
+    return buffers; two one-element all-reduces order the phases. No host synchronisation."""
+    C = bufs._C
+    world, rank = bufs.world, bufs.rank
+    T, H = hidden.shape
+    E = router_logits.size(1)
+    el = E // world
+    assert T <= bufs.max_tokens and H == bufs.hidden and top_k == bufs.top_k, "EPBuffers too small"
+    assert E == bufs.num_experts and hidden.dtype == bufs.dtype
+    ids, w, tpe, scratch = C.moe_route(router_logits, top_k)
+    counts_all = torch.empty(world, E, dtype=torch.int64, device=hidden.device)
+    dist.all_gather_into_tensor(counts_all, tpe, group=bufs.group)
+    slot_pos = C.ep_dispatch(hidden, ids, scratch, counts_all, rank, bufs.ptrs["recv"],
+                             bufs.ptrs["origin"])
+    bufs.fence()
+    seg_counts = counts_all[:, rank * el:(rank + 1) * el].contiguous().view(-1)
+    h = C.ep_grouped_gemm(bufs.recv, w_gate_up, seg_counts, el, True, None, [], sort_by_m)
+    C.ep_grouped_gemm(h, w_down, seg_counts, el, False, bufs.origin, bufs.ptrs["back"],
+                      sort_by_m)
+    bufs.fence()
+    return C.moe_combine(bufs.back[:T * top_k], w, slot_pos)
+
+
 def _check(hidden, router_logits, w_gate_up, w_down, top_k, world):
     assert hidden.dim() == 2 and router_logits.dim() == 2
     assert w_gate_up.dim() == 3 and w_down.dim() == 3
@@ -83,6 +181,7 @@ def fused_moe(
     ep_group: Optional[dist.ProcessGroup] = None,
     sort_by_m: bool = True,
     ops: Optional[MoEOps] = None,
+    ep_buffers: Optional[EPBuffers] = None,
 ) -> torch.Tensor:
     """MoE layer forward.
 
@@ -95,11 +194,16 @@ def fused_moe(
         ep_group: expert-parallel process group (None: single GPU, E_local = E).
         sort_by_m: heaviest-expert-first tile order inside the grouped GEMMs.
         ops: compute stages (defaults to the CUDA kernels).
+        ep_buffers: EPBuffers of `ep_group`: selects the fused peer-memory path (dispatch and
+            result scatter over NVLink inside the kernels) instead of NCCL all-to-alls.
 
     Returns: [T, H] = sum_j w[t,j] * down(silu(gate(x_t)) * up(x_t)) for the top-k experts.
     """
     world = dist.get_world_size(ep_group) if ep_group is not None else 1
     T, H, E, el = _check(hidden, router_logits, w_gate_up, w_down, top_k, world)
+    if ep_buffers is not None and world > 1 and ops is None:
+        return _fused_moe_p2p(hidden.contiguous(), router_logits, w_gate_up, w_down, top_k,
+                              ep_buffers, sort_by_m)
     if ops is None:
         ops = cuda_ops()
     hidden = hidden.contiguous()

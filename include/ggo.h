@@ -140,6 +140,47 @@ int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
                     const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden, int top_k,
                     void* out_dev, int dtype, cudaStream_t stream);
 
+/* ----------------------------------------------------------------- expert parallelism
+ * The fused expert-parallel path over NVLink peer memory. None of these has a counterpart in the
+ * reference, which is single-device. Buffers are shared between the ranks of one node through
+ * CUDA IPC (ggo_ipc_*): every rank allocates its receive buffers, exchanges the 64-byte handles
+ * (e.g. with an all_gather of bytes) and opens its peers' handles; kernels then load and store
+ * peer memory directly. Ordering between ranks is the caller's: a collective (e.g. a one-element
+ * NCCL all-reduce) after ggo_ep_dispatch and after the scattering GEMM. */
+#define GGO_IPC_HANDLE_BYTES 64
+#define GGO_MAX_EP_RANKS 8
+
+/* cudaMalloc `bytes` and return its IPC handle (GGO_IPC_HANDLE_BYTES bytes into handle_out). */
+int ggo_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out);
+/* Map a peer's buffer from its handle (peer access enabled lazily). */
+int ggo_ipc_open(const void* handle, void** ptr_out);
+int ggo_ipc_close(void* peer_ptr);
+int ggo_ipc_free(void* ptr);
+
+/* Expert-parallel dispatch: ggo_moe_permute that writes every routed row straight into the
+ * receive buffer of the rank owning its expert (rank r owns experts [r*E/P, (r+1)*E/P)).
+ * counts_all_dev [P, E] int64: every rank's tokens_per_expert (e.g. an all_gather of them).
+ * recv_rows[r] / recv_origin[r]: rank r's receive rows [capacity, H] and origin [capacity] int32,
+ * as mapped in this process (own buffers for r == rank). Received rows are laid out as
+ * [source rank][local expert] segments; recv_origin holds each row's sorted position on its
+ * source rank. slot_pos_dev as in ggo_moe_permute. */
+int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int num_experts,
+                    int top_k, const int32_t* topk_ids_dev, const void* scratch_dev,
+                    const int64_t* counts_all_dev, int world_size, int rank,
+                    void* const* recv_rows, int32_t* const* recv_origin, int32_t* slot_pos_dev,
+                    int dtype, cudaStream_t stream);
+
+/* Grouped GEMM over a receive buffer of capacity_rows rows whose segment counts (device) may sum
+ * to less. swiglu != 0: the gate/up SwiGLU form (N = F, weights [E, 2F, K]). With origin_dev set
+ * (scatter epilogue), row r's result is stored to peer_out[(segment of r) / num_experts] +
+ * origin_dev[r] * N, i.e. straight back to the source rank's buffer over NVLink, and
+ * output_dev may be NULL. world_size = number of peer_out entries. */
+int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,
+                        const int64_t* tokens_per_segment_dev, int num_segments, int num_experts,
+                        int64_t capacity_rows, int64_t N, int64_t K, int dtype, int swiglu,
+                        const int32_t* origin_dev, void* const* peer_out, int world_size,
+                        int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
 /* Grouped GEMM that allocates nothing: same arguments, result and validation as
  * ggo_grouped_gemm, minus the workspace. It has no counterpart in the reference; it exists for
  * callers that cannot call cudaMalloc themselves or hand over a buffer -- code running while a

@@ -21,7 +21,7 @@ def main():
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    from grouped_gemm_opt import fused_moe
+    from grouped_gemm_opt import EPBuffers, fused_moe
     g = torch.Generator(device="cuda").manual_seed(0)
     x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
     logits = torch.randn(T, E, device="cuda", generator=g)
@@ -32,11 +32,19 @@ def main():
     out = fused_moe(xs, ls, wgu[rank * el:(rank + 1) * el].contiguous(),
                     wd[rank * el:(rank + 1) * el].contiguous(), k, ep_group=dist.group.WORLD)
     ref = fused_moe(xs, ls, wgu, wd, k)
+    bufs = EPBuffers(dist.group.WORLD, tl, H, k, E, torch.bfloat16)
+    wgl = wgu[rank * el:(rank + 1) * el].contiguous()
+    wdl = wd[rank * el:(rank + 1) * el].contiguous()
+    outs_p2p = [fused_moe(xs, ls, wgl, wdl, k, ep_group=dist.group.WORLD, ep_buffers=bufs)
+                for _ in range(2)]  # twice: buffers are reused across layers
     torch.cuda.synchronize()
-    d = (out.float() - ref.float()).abs().max().item()
-    rel = d / max(ref.float().abs().max().item(), 1e-12)
-    assert out.shape == ref.shape and rel <= 1e-2, rel
-    print(f"EP_OK {rank} {rel:.3e}", flush=True)
+    rels = []
+    for o in [out] + outs_p2p:
+        d = (o.float() - ref.float()).abs().max().item()
+        rels.append(d / max(ref.float().abs().max().item(), 1e-12))
+        assert o.shape == ref.shape and rels[-1] <= 1e-2, rels
+    bufs.close()
+    print(f"EP_OK {rank} " + " ".join(f"{r:.3e}" for r in rels), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

@@ -40,7 +40,7 @@ def test_metadata_calls(lib):
     assert lib.ggo_workspace_size() == 256
     lib.ggo_moe_route_scratch_bytes.restype = ctypes.c_size_t
     lib.ggo_moe_route_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int]
-    assert lib.ggo_moe_route_scratch_bytes(16384, 8) == 128 * 8 * 4
+    assert lib.ggo_moe_route_scratch_bytes(16384, 8) == (16384 // 32 + 1) * 8 * 4
 
 
 def _gemm(lib, a=1 << 20, b=1 << 20, c=1 << 20, cnt=1 << 20, e=8, t=256, n=1024, k=512, dt=0,
