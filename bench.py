@@ -217,10 +217,12 @@ def run_reference(args):
 
 def moe_layer_bench(world, rank, steps, warmup):
     """Expert-parallel Mixtral layer: T=16384 tokens in total (split over ranks), H=4096,
-    F=14336, E=8, top-2. Returns tokens/s of the whole job (max-over-ranks device time)."""
+    F=14336, E=8, top-2. Returns tokens/s of the whole job (max-over-ranks device time). With
+    N>1 the headline uses the fused peer-memory path (EPBuffers); the NCCL all-to-all path is
+    reported beside it."""
     import torch
     import torch.distributed as dist
-    from grouped_gemm_opt import fused_moe
+    from grouped_gemm_opt import EPBuffers, fused_moe
     T, H, F, Ex, k = 16384, 4096, 14336, 8, 2
     el = Ex // world
     tl = T // world
@@ -230,17 +232,30 @@ def moe_layer_bench(world, rank, steps, warmup):
     wgu = (torch.randn(el, 2 * F, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     wd = (torch.randn(el, H, F, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     grp = dist.group.WORLD if world > 1 else None
-    fn = lambda: fused_moe(x, logits, wgu, wd, k, ep_group=grp)  # noqa: E731
-    for _ in range(warmup):
-        fn()
-    total_ms, _ = _timed(fn, steps, world)
     flops = 6.0 * T * k * H * F
-    return {"metric": "moe_layer_tokens_per_s", "value": T * steps / (total_ms / 1e3),
-            "unit": "tokens/s", "ms_per_step": total_ms / steps,
-            "tflops": flops * steps / (total_ms / 1e3) / 1e12,
-            "config": {"workload": "Mixtral MoE layer T16384 H4096 F14336 E8 top2",
-                       "parallelism": f"ep{world}", "scaling": "strong"},
-            "kernels_per_step": 5 if world == 1 else 5}
+    res = {}
+    bufs = EPBuffers(grp, tl, H, k, Ex, torch.bfloat16) if world > 1 else None
+    paths = [("p2p", bufs), ("nccl", None)] if world > 1 else [("single", None)]
+    for name, b in paths:
+        fn = lambda: fused_moe(x, logits, wgu, wd, k, ep_group=grp, ep_buffers=b)  # noqa: E731
+        for _ in range(warmup):
+            fn()
+        total_ms, _ = _timed(fn, steps, world)
+        res[name] = total_ms / steps
+    if bufs is not None:
+        bufs.close()
+    best = "p2p" if world > 1 else "single"
+    ms = res[best]
+    out = {"metric": "moe_layer_tokens_per_s", "value": T / (ms / 1e3),
+           "unit": "tokens/s", "ms_per_step": ms, "tflops": flops / (ms / 1e3) / 1e12,
+           "path": {"p2p": "fused dispatch/scatter over NVLink peer memory (CUDA IPC)",
+                    "single": "one GPU, no collectives"}[best],
+           "config": {"workload": "Mixtral MoE layer T16384 H4096 F14336 E8 top2",
+                      "parallelism": f"ep{world}", "scaling": "strong"},
+           "kernels_per_step": 6}
+    if world > 1:
+        out["nccl_all_to_all_value"] = T / (res["nccl"] / 1e3)
+    return out
 
 
 def profile_run(args):
