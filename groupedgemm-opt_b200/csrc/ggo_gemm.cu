@@ -46,18 +46,30 @@ int get_encode(EncodeTiledFn* fn) {
 
 // 2D K-major operand map: dims {K, rows}, box {64, box_rows}, 128-B swizzle, zero fill out of
 // bounds.
-int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows) {
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
+             int box_cols = kBK) {
   EncodeTiledFn enc;
   if (int st = get_encode(&enc)) return st;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                    const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? GGO_OK : GGO_ERR_CUDA;
+}
+
+// Output map for the TMA-store epilogue: [rows, n_out] row-major, boxes of 32 rows x 64 columns
+// (128 B, 128-B swizzle, matching the staging layout). Only for a plain (non-scattered) output.
+int make_out_map(CUtensorMap* m, GemmParams* p, bool bf16) {
+  memset(m, 0, sizeof(*m));
+  p->use_tma_store = 0;
+  if (p->out == nullptr || p->origin != nullptr) return GGO_OK;
+  if (int st = make_map(m, p->out, p->rows, p->n_out, bf16, 32, 64)) return st;
+  p->use_tma_store = 1;
+  return GGO_OK;
 }
 
 // Per (device, kernel) one-time set-up: the dynamic shared-memory opt-in and, for cluster
@@ -92,9 +104,11 @@ int kernel_setup(Kern kern, int smem, int dev, bool pair, int* resident) {
 template <int BN, int EPI, bool BF16>
 int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
            cudaStream_t stream) {
-  CUtensorMap ma, mb;
-  if (int st = make_map(&ma, a, p.rows, p.k, BF16, kBM)) return st;
-  if (int st = make_map(&mb, b, b_rows, p.k, BF16, 128)) return st;
+  CUtensorMap ma, mb, mc;
+  GemmParams q = p;
+  if (int st = make_map(&ma, a, q.rows, q.k, BF16, kBM)) return st;
+  if (int st = make_map(&mb, b, b_rows, q.k, BF16, 128)) return st;
+  if (int st = make_out_map(&mc, &q, BF16)) return st;
   auto kern = grouped_gemm_kernel<BN, EPI, BF16>;
   constexpr int smem = SmemLayout<BN>::kTotal;
   int sms = 0;
@@ -104,16 +118,18 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   const int64_t ub = ((p.rows + kBM - 1) / kBM + p.num_segments) * n_tiles;  // tile upper bound
   const int grid = static_cast<int>(ub < sms ? ub : sms);
   if (grid <= 0) return GGO_OK;
-  kern<<<grid, kThreads, smem, stream>>>(ma, mb, p);
+  kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, q);
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 
 template <int BN, int EPI, bool BF16>
 int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
                 cudaStream_t stream) {
-  CUtensorMap ma, mb;
-  if (int st = make_map(&ma, a, p.rows, p.k, BF16, 128)) return st;
-  if (int st = make_map(&mb, b, b_rows, p.k, BF16, BN / 2)) return st;
+  CUtensorMap ma, mb, mc;
+  GemmParams q = p;
+  if (int st = make_map(&ma, a, q.rows, q.k, BF16, 128)) return st;
+  if (int st = make_map(&mb, b, b_rows, q.k, BF16, BN / 2)) return st;
+  if (int st = make_out_map(&mc, &q, BF16)) return st;
   auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16>;
   constexpr int smem = PairLayout<BN>::kTotal;
   int clusters = 0;
@@ -123,7 +139,7 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
   const int64_t ub = ((p.rows + 255) / 256 + p.num_segments) * n_tiles;  // pair-tile upper bound
   const int64_t pairs = ub < clusters ? ub : clusters;
   if (pairs <= 0) return GGO_OK;
-  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, p);
+  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, mc, q);
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 

@@ -75,6 +75,7 @@ struct GemmParams {
   // peer_out[segment / num_experts] + origin[r] * n_out instead of out + r * n_out.
   const int32_t* origin;
   void* peer_out[8];
+  int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
   GgoWorkspace* ws;
 };
 
@@ -95,9 +96,11 @@ struct SmemLayout {
   static constexpr int kBBytes = BN * kBK * 2;    // 32 KB or 16 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTileBytes = kStages * kStageBytes;
+  static constexpr int kStagingBytes = 4 * 4096;  // TMA-store staging, 4 KB per epilogue warp
   static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
-  static constexpr int kTotal = 1024 /*align slack*/ + kTileBytes + kTableBytes + kMiscBytes;
+  static constexpr int kTotal =
+      1024 /*align slack*/ + kTileBytes + kStagingBytes + kTableBytes + kMiscBytes;
 };
 
 // Builds, in shared memory, the segment table every CTA needs to map a flat tile index to work:
@@ -234,76 +237,96 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
   return info;
 }
 
-// Epilogue for one accumulator row held by this thread: TMEM columns [0, BN) of lane quarter
-// `t_row` -> (optional SwiGLU) -> bf16/fp16 -> 16-byte global stores of output columns
-// n0 + [0, BN or BN/2). All 32 lanes of the warp must call it (tcgen05.ld is warp-collective).
-template <int BN, int EPI, bool BF16, typename OutT>
-__device__ __forceinline__ void store_tile_row(uint32_t t_row, int n0, int n_out, bool row_ok,
-                                               OutT* out_row) {
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&t2);
+  }
+  __half2 t2 = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t2);
+}
+
+// 32 output columns of this thread's accumulator row, packed as 16 bf16x2/half2 words: TMEM
+// columns [c, c+32) (plain), or silu(gate) * up from columns [c, c+32) and [BN/2 + c, ...).
+template <int BN, int EPI, bool BF16>
+__device__ __forceinline__ void load_out32(uint32_t t_row, int c, uint32_t (&o)[16]) {
   if (EPI == kEpiStore) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(t_row + c, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      o[i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]), BF16);
+  } else {
+    uint32_t g[32], u[32];
+    tmem_ld_32x32b_x32(t_row + c, g);
+    tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float gv = __uint_as_float(g[2 * i + e]);
+        const float uv = __uint_as_float(u[2 * i + e]);
+        y[e] = gv / (1.0f + __expf(-gv)) * uv;
+      }
+      o[i] = pack2(y[0], y[1], BF16);
+    }
+  }
+}
+
+// Epilogue of one warp's 32 accumulator rows (one row per thread, TMEM lane quarter `t_row`):
+// output columns n0 + [0, OUTW), OUTW = BN (plain) or BN / 2 (SwiGLU). All 32 lanes must call it
+// (tcgen05.ld is warp-collective).
+//  * warp_tma: the warp's 32 rows all belong to the tile's segment and an output tensor map
+//    exists. Each 64-column box is staged in `stage` (4 KB, 1024-B aligned, rows of 128 B with
+//    the 128-B swizzle: 16-B chunk j of row r at chunk j ^ (r % 8), conflict-free) and written
+//    with one TMA store; the box at x0 = n0 + c64, y0 = x_row0. Columns past n_out are clipped by
+//    the tensor map.
+//  * otherwise each thread stores its own row with 16-byte stores, masked by row_ok and n_out.
+template <int BN, int EPI, bool BF16, typename OutT>
+__device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_out, bool row_ok,
+                                                OutT* out_row, bool warp_tma,
+                                                const CUtensorMap* tmC, uint8_t* stage,
+                                                int x_row0) {
+  constexpr int OUTW = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  const int lane = threadIdx.x & 31;
+  const uint32_t st_row = smem_u32(stage) + lane * 128;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c, v);
-      tmem_ld_wait();
-      if (row_ok) {
+  for (int c64 = 0; c64 < OUTW; c64 += 64) {
+    if (warp_tma && c64 > 0) {  // the previous box's store has read the staging buffer
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+    }
+#pragma unroll 1
+    for (int s = 0; s < 2; ++s) {
+      const int c = c64 + 32 * s;
+      if (c >= OUTW) break;
+      uint32_t o[16];
+      load_out32<BN, EPI, BF16>(t_row, c, o);
+      if (warp_tma) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int col = n0 + c + 8 * j;
-          if (col < n_out) {
-            uint4 pk;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t chunk = static_cast<uint32_t>((4 * s + q) ^ (lane & 7));
+          st_shared_v4(st_row + chunk * 16, o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+      } else if (row_ok) {
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float a = __uint_as_float(v[8 * j + 2 * h]);
-              const float b = __uint_as_float(v[8 * j + 2 * h + 1]);
-              if (BF16) {
-                __nv_bfloat162 t2 = __floats2bfloat162_rn(a, b);
-                w[h] = *reinterpret_cast<uint32_t*>(&t2);
-              } else {
-                __half2 t2 = __floats2half2_rn(a, b);
-                w[h] = *reinterpret_cast<uint32_t*>(&t2);
-              }
-            }
-            *reinterpret_cast<uint4*>(out_row + col) = pk;
-          }
+        for (int q = 0; q < 4; ++q) {
+          const int col = n0 + c + 8 * q;
+          if (col < n_out)
+            *reinterpret_cast<uint4*>(out_row + col) =
+                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
         }
       }
     }
-  } else {
-#pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
-      uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(t_row + c, g);
-      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
-      tmem_ld_wait();
-      if (row_ok) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int col = n0 + c + 8 * j;
-          if (col < n_out) {
-            uint4 pk;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              float y[2];
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const float gv = __uint_as_float(g[8 * j + 2 * h + e]);
-                const float uv = __uint_as_float(u[8 * j + 2 * h + e]);
-                y[e] = gv / (1.0f + __expf(-gv)) * uv;
-              }
-              if (BF16) {
-                __nv_bfloat162 t2 = __floats2bfloat162_rn(y[0], y[1]);
-                w[h] = *reinterpret_cast<uint32_t*>(&t2);
-              } else {
-                __half2 t2 = __floats2half2_rn(y[0], y[1]);
-                w[h] = *reinterpret_cast<uint32_t*>(&t2);
-              }
-            }
-            *reinterpret_cast<uint4*>(out_row + col) = pk;
-          }
-        }
+    if (warp_tma) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, stage, n0 + c64, x_row0);
+        bulk_commit();
       }
     }
   }
@@ -324,21 +347,24 @@ __device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo&
 template <int BN, int EPI, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using L = SmemLayout<BN>;
   constexpr int S = L::kStages;
   constexpr int kTmemCols = 2 * BN;             // two accumulators
   constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  constexpr bool kTmaStoreOk = kOutBN % 64 == 0;  // output boxes are 64 columns wide
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
-  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
+  uint8_t* staging = smem + L::kTileBytes;
+  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes + L::kStagingBytes);
   int* t_rowoff = t_cnt + kMaxSegments;
   int* t_order = t_rowoff + kMaxSegments;
   int* t_tileoff = t_order + kMaxSegments;  // kMaxSegments + 1 entries
-  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
+  uint8_t* misc = smem + L::kTileBytes + L::kStagingBytes + L::kTableBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* accf_bar = empty_bar + S;
@@ -473,7 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
-      store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
+      const bool warp_tma = kTmaStoreOk && p.use_tma_store && ew * 32 + 32 <= info.rows;
+      store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
+                                     staging + ew * 4096, info.row0 + ew * 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
@@ -483,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------------------------ tear-down
   if (p.origin) __threadfence_system();  // scattered rows visible to the peers before exit
+  if (warp >= 4 && lane == 0) bulk_wait_all();  // TMA stores done before shared memory goes
   __syncthreads();
   if (warp == 2) {
     tc_fence_after();

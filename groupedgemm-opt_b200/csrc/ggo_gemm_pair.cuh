@@ -27,15 +27,17 @@ struct PairLayout {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (200 * 1024 / kStageBytes) > 8 ? 8 : (200 * 1024 / kStageBytes);
   static constexpr int kTileBytes = kStages * kStageBytes;
+  static constexpr int kStagingBytes = 4 * 4096;  // TMA-store staging, 4 KB per epilogue warp
   static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
-  static constexpr int kTotal = 1024 + kTileBytes + kTableBytes + kMiscBytes;
+  static constexpr int kTotal = 1024 + kTileBytes + kStagingBytes + kTableBytes + kMiscBytes;
 };
 
 template <int BN, int EPI, bool BF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                             const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                             const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using L = PairLayout<BN>;
   constexpr int S = L::kStages;
   // BN = N of the pair tile = columns of each CTA's accumulator (multiple of 32, <= 256)
@@ -44,16 +46,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int kAccStride = 256;        // TMEM columns between the two accumulators
   constexpr int kTmemCols = 512;
   constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  constexpr bool kTmaStoreOk = kOutBN % 64 == 0;  // output boxes are 64 columns wide
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
-  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes);
+  uint8_t* staging = smem + L::kTileBytes;
+  int* t_cnt = reinterpret_cast<int*>(smem + L::kTileBytes + L::kStagingBytes);
   int* t_rowoff = t_cnt + kMaxSegments;
   int* t_order = t_rowoff + kMaxSegments;
   int* t_tileoff = t_order + kMaxSegments;
-  uint8_t* misc = smem + L::kTileBytes + L::kTableBytes;
+  uint8_t* misc = smem + L::kTileBytes + L::kStagingBytes + L::kTableBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* accf_bar = empty_bar + S;
@@ -204,7 +208,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * kAccStride;
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
-      store_tile_row<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row);
+      const int wrow0 = static_cast<int>(rank) * 128 + ew * 32;
+      const bool warp_tma = kTmaStoreOk && p.use_tma_store && wrow0 + 32 <= info.rows;
+      store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
+                                     staging + ew * 4096, info.row0 + wrow0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));
@@ -214,6 +221,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------------------------ tear-down
   if (p.origin) __threadfence_system();  // scattered rows visible to the peers before exit
+  if (warp >= 4 && lane == 0) bulk_wait_all();  // TMA stores done before shared memory goes
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no remote arrive or ring store may target a CTA that has exited
