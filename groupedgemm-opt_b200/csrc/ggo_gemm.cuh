@@ -101,6 +101,7 @@ struct SmemLayout {
   static constexpr int kMiscBytes = 1024;
   static constexpr int kTotal =
       1024 /*align slack*/ + kTileBytes + kStagingBytes + kTableBytes + kMiscBytes;
+  static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
 // Builds, in shared memory, the segment table every CTA needs to map a flat tile index to work:

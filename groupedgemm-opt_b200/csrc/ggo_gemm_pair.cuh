@@ -25,12 +25,15 @@ struct PairLayout {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 A rows
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of the BN-row B tile
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (200 * 1024 / kStageBytes) > 8 ? 8 : (200 * 1024 / kStageBytes);
-  static constexpr int kTileBytes = kStages * kStageBytes;
   static constexpr int kStagingBytes = 4 * 4096;  // TMA-store staging, 4 KB per epilogue warp
   static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
+  // as many stages (<= 8) as fit in the 227 KB a CTA may use, after everything else
+  static constexpr int kRingBudget = 227 * 1024 - 1024 - kStagingBytes - kTableBytes - kMiscBytes;
+  static constexpr int kStages = (kRingBudget / kStageBytes) > 8 ? 8 : (kRingBudget / kStageBytes);
+  static constexpr int kTileBytes = kStages * kStageBytes;
   static constexpr int kTotal = 1024 + kTileBytes + kStagingBytes + kTableBytes + kMiscBytes;
+  static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
 template <int BN, int EPI, bool BF16>
