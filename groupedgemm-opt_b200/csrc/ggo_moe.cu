@@ -98,29 +98,53 @@ __global__ void __launch_bounds__(kRouteThreads)
 
 // One block of 1024 threads. Turns block_counts[b][e] into absolute start rows (in place),
 // writes tokens_per_expert and the exclusive start row of every expert (expert_start[E], stored
-// right after the nblocks x E table).
+// right after the nblocks x E table). Each expert's column of the table is split into
+// P = 1024 / E contiguous block ranges, one per thread: range sums, a per-expert scan of the P
+// partial sums, a scan over experts, then every thread rewrites its range.
 __global__ void __launch_bounds__(1024)
     route_scan_kernel(int* __restrict__ block_counts, int nblocks, int E,
                       int64_t* __restrict__ tpe) {
-  int* expert_start = block_counts + static_cast<size_t>(nblocks) * E;
+  __shared__ int part[1024];   // [E][P] range sums, then exclusive range offsets within expert
   __shared__ int tot[kMaxExperts];
-  const int e = threadIdx.x;
+  int* expert_start = block_counts + static_cast<size_t>(nblocks) * E;
+  const int P = max(1, 1024 / E);
+  const int tid = threadIdx.x;
+  const int e = tid / P, q = tid % P;
+  const bool active = e < E;
+  const int per = (nblocks + P - 1) / P;
+  const int b0 = min(nblocks, q * per), b1 = min(nblocks, b0 + per);
   int sum = 0;
-  if (e < E)
-    for (int b = 0; b < nblocks; ++b) sum += block_counts[static_cast<size_t>(b) * E + e];
-  tot[e] = e < E ? sum : 0;
+  if (active)
+    for (int b = b0; b < b1; ++b) sum += block_counts[static_cast<size_t>(b) * E + e];
+  part[tid] = sum;
   __syncthreads();
-  for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
-    const int v = e >= o ? tot[e - o] : 0;
+  if (tid < E) {  // exclusive scan of expert tid's P range sums
+    int run = 0;
+    for (int j = 0; j < P; ++j) {
+      const int v = part[tid * P + j];
+      part[tid * P + j] = run;
+      run += v;
+    }
+    tot[tid] = run;
+  }
+  __syncthreads();
+  // exclusive scan over experts (E <= 1024): inclusive Hillis-Steele on a copy
+  __shared__ int inc[kMaxExperts];
+  if (tid < kMaxExperts) inc[tid] = tid < E ? tot[tid] : 0;
+  __syncthreads();
+  for (int o = 1; o < kMaxExperts; o <<= 1) {
+    const int v = (tid < kMaxExperts && tid >= o) ? inc[tid - o] : 0;
     __syncthreads();
-    tot[e] += v;
+    if (tid < kMaxExperts) inc[tid] += v;
     __syncthreads();
   }
-  if (e < E) {
-    int run = tot[e] - sum;  // exclusive start of expert e
-    tpe[e] = sum;
-    expert_start[e] = run;
-    for (int b = 0; b < nblocks; ++b) {
+  if (tid < E) {
+    tpe[tid] = tot[tid];
+    expert_start[tid] = inc[tid] - tot[tid];
+  }
+  if (active) {
+    int run = inc[e] - tot[e] + part[tid];
+    for (int b = b0; b < b1; ++b) {
       const size_t i = static_cast<size_t>(b) * E + e;
       const int c = block_counts[i];
       block_counts[i] = run;

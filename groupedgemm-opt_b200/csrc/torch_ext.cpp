@@ -9,6 +9,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <algorithm>
+#include <array>
 #include <map>
 #include <mutex>
 #include <string>
@@ -193,6 +195,106 @@ int64_t workspace_error(int64_t device) {
   return code;
 }
 
+// ------------------------------------------------------------------ host-buffer pipeline
+// Three persistent non-blocking streams per device: copies in, grouped GEMMs, copies out.
+std::mutex g_side_mu;
+std::map<int, std::array<cudaStream_t, 3>> g_side_streams;
+
+std::array<cudaStream_t, 3> side_streams(int dev) {
+  std::lock_guard<std::mutex> lk(g_side_mu);
+  auto it = g_side_streams.find(dev);
+  if (it == g_side_streams.end()) {
+    std::array<cudaStream_t, 3> s{};
+    for (auto& x : s)
+      TORCH_CHECK(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) == cudaSuccess,
+                  "stream creation failed");
+    it = g_side_streams.emplace(dev, s).first;
+  }
+  return it->second;
+}
+
+// Grouped GEMM on host-resident activations (see grouped_gemm_opt_host): expert groups of about
+// T/chunks rows are copied in, multiplied and copied back on three streams so the stages of
+// consecutive groups overlap. Inputs/outputs should be pinned for the copies to be asynchronous.
+// All work is joined back to the current stream before returning (nothing waits on the host).
+torch::Tensor grouped_gemm_host(const torch::Tensor& input, const torch::Tensor& weights,
+                                const torch::Tensor& tokens_per_expert, torch::Tensor out,
+                                int64_t tile_config, bool sort_by_m, int64_t chunks) {
+  TORCH_CHECK(!input.is_cuda() && input.dim() == 2 && input.is_contiguous(),
+              "input must be a contiguous 2D host tensor");
+  TORCH_CHECK(weights.is_cuda() && weights.dim() == 3 && weights.is_contiguous(),
+              "weights must be a contiguous 3D CUDA tensor");
+  TORCH_CHECK(input.size(1) == weights.size(2), "K mismatch");
+  TORCH_CHECK(input.scalar_type() == weights.scalar_type(), "input/weights dtype mismatch");
+  auto tpe = tokens_per_expert.to(torch::kInt64).cpu().contiguous();
+  const int64_t T = input.size(0), K = input.size(1), E = weights.size(0), N = weights.size(1);
+  TORCH_CHECK(tpe.numel() == E, "tokens_per_expert must have num_experts entries");
+  const int64_t* c = tpe.data_ptr<int64_t>();
+  int64_t total = 0;
+  for (int64_t e = 0; e < E; ++e) total += c[e];
+  TORCH_CHECK(total == T, "sum(tokens_per_expert)=", total, " != total_tokens=", T);
+  TORCH_CHECK(out.defined() && !out.is_cuda() && out.is_contiguous() && out.size(0) == T &&
+                  out.size(1) == N && out.scalar_type() == input.scalar_type(),
+              "out must be a contiguous host tensor [T, N] of the input dtype");
+  if (T == 0) return out;
+  c10::cuda::CUDAGuard guard(weights.device());
+  const int dev = weights.device().index();
+  cudaStream_t cur = at::cuda::getCurrentCUDAStream();
+  auto ss = side_streams(dev);
+  cudaStream_t s_in = ss[0], s_mm = ss[1], s_out = ss[2];
+  const size_t esz = input.element_size();
+  auto dopt = input.options().device(weights.device());
+  auto d_x = torch::empty({T, K}, dopt);
+  auto d_y = torch::empty({T, N}, dopt);
+  auto d_c = torch::empty({E}, torch::TensorOptions().dtype(torch::kInt64).device(weights.device()));
+  std::vector<cudaEvent_t> evs;
+  auto event = [&](cudaStream_t s) {
+    cudaEvent_t ev;
+    TORCH_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess, "event");
+    TORCH_CHECK(cudaEventRecord(ev, s) == cudaSuccess, "event record");
+    evs.push_back(ev);
+    return ev;
+  };
+  cudaEvent_t e0 = event(cur);
+  for (cudaStream_t s : {s_in, s_mm, s_out}) cudaStreamWaitEvent(s, e0, 0);
+  TORCH_CHECK(cudaMemcpyAsync(d_c.data_ptr(), c, E * 8, cudaMemcpyHostToDevice, s_in) ==
+                  cudaSuccess, "count copy");
+  const int64_t nch = std::max<int64_t>(1, chunks);
+  int64_t e_begin = 0, row = 0;
+  const int dt = dtype_code(input);
+  void* ws = workspace_for(weights.device(), s_mm);
+  for (int64_t ch = 0; ch < nch && e_begin < E; ++ch) {
+    // next group: experts until the group holds about T / nch rows (the last takes the rest)
+    int64_t e_end = e_begin, rows = 0;
+    const int64_t target = (T * (ch + 1)) / nch - row;
+    while (e_end < E && (rows < target || ch == nch - 1)) rows += c[e_end++];
+    if (rows == 0) { e_begin = e_end; continue; }
+    const char* src = static_cast<const char*>(input.data_ptr()) + row * K * esz;
+    char* dx = static_cast<char*>(d_x.data_ptr()) + row * K * esz;
+    char* dy = static_cast<char*>(d_y.data_ptr()) + row * N * esz;
+    TORCH_CHECK(cudaMemcpyAsync(dx, src, rows * K * esz, cudaMemcpyHostToDevice, s_in) ==
+                    cudaSuccess, "input copy");
+    cudaStreamWaitEvent(s_mm, event(s_in), 0);
+    const char* wptr = static_cast<const char*>(weights.data_ptr()) + e_begin * N * K * esz;
+    const int st = ggo_grouped_gemm_segments(
+        dx, wptr, dy, d_c.data_ptr<int64_t>() + e_begin, static_cast<int>(e_end - e_begin),
+        static_cast<int>(e_end - e_begin), rows, N, K, dt, static_cast<int>(tile_config),
+        sort_by_m ? 1 : 0, ws, s_mm);
+    check_status(st, "grouped GEMM (host pipeline)");
+    cudaStreamWaitEvent(s_out, event(s_mm), 0);
+    char* dst = static_cast<char*>(out.data_ptr()) + row * N * esz;
+    TORCH_CHECK(cudaMemcpyAsync(dst, dy, rows * N * esz, cudaMemcpyDeviceToHost, s_out) ==
+                    cudaSuccess, "output copy");
+    row += rows;
+    e_begin = e_end;
+  }
+  for (cudaStream_t s : {s_in, s_mm, s_out}) cudaStreamWaitEvent(cur, event(s), 0);
+  for (cudaEvent_t ev : evs) cudaEventDestroy(ev);
+  // the device buffers are freed to the caching allocator on `cur`, which now waits for all
+  // side-stream work, so they cannot be reused early
+  return out;
+}
+
 // ------------------------------------------------------------------ expert parallelism (IPC)
 // Allocates `nbytes` of device memory shareable with the other processes of the node; returns
 // (address, 64-byte handle).
@@ -306,6 +408,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("slot_pos"));
   m.def("workspace_error", &workspace_error, py::arg("device") = 0);
   m.def("abi_version", []() { return ggo_version(); });
+  m.def("grouped_gemm_host", &grouped_gemm_host, py::arg("input"), py::arg("weights"),
+        py::arg("tokens_per_expert"), py::arg("out"), py::arg("tile_config") = 4,
+        py::arg("sort_by_m") = true, py::arg("chunks") = 4);
   m.def("ipc_alloc", &ipc_alloc, py::arg("nbytes"));
   m.def("ipc_open", &ipc_open, py::arg("handle"));
   m.def("ipc_close", &ipc_close, py::arg("ptr"));

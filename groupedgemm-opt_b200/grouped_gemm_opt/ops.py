@@ -97,50 +97,10 @@ def grouped_gemm_opt_host(
     (allocated pinned if not given) after the stream work is enqueued; it is complete once the
     current stream is synchronised (all work is joined back to it).
     """
-    from grouped_gemm_opt._native import _C
-
     assert weights.is_cuda and weights.dim() == 3 and input.dim() == 2
     assert not input.is_cuda, "input must be in host memory (pin it for overlap)"
-    tpe = tokens_per_expert.to(torch.int64).cpu()
-    T, K = input.shape
-    E, N = weights.size(0), weights.size(1)
-    assert int(tpe.sum()) == T, f"sum(tokens_per_expert)={int(tpe.sum())} != total_tokens={T}"
     if out is None:
-        out = torch.empty(T, N, dtype=input.dtype, pin_memory=True)
-    if T == 0:
-        return out
-    dev = weights.device
-    main = torch.cuda.current_stream(dev)
-    s_in, s_mm, s_out = (torch.cuda.Stream(dev) for _ in range(3))
-    for s in (s_in, s_mm, s_out):
-        s.wait_stream(main)
-    # contiguous expert groups with about T/chunks rows each
-    bounds, acc, target = [0], 0, T / max(1, chunks)
-    for e in range(E):
-        acc += int(tpe[e])
-        if acc >= target * len(bounds) and e + 1 < E and len(bounds) < chunks:
-            bounds.append(e + 1)
-    bounds.append(E)
-    offs = torch.cat([torch.zeros(1, dtype=torch.int64), torch.cumsum(tpe, 0)])
-    weights = weights.contiguous()
-    keep = []
-    for e0, e1 in zip(bounds[:-1], bounds[1:]):
-        r0, r1 = int(offs[e0]), int(offs[e1])
-        if r1 == r0:
-            continue
-        with torch.cuda.stream(s_in):
-            xd = input[r0:r1].to(dev, non_blocking=True)
-            cd = tpe[e0:e1].to(dev, non_blocking=True)
-        s_mm.wait_stream(s_in)
-        with torch.cuda.stream(s_mm):
-            yd = _C.grouped_gemm_segments(xd, weights[e0:e1], cd, e1 - e0, int(tile_config),
-                                          sort_by_m)
-        s_out.wait_stream(s_mm)
-        with torch.cuda.stream(s_out):
-            out[r0:r1].copy_(yd, non_blocking=True)
-        for t, s in ((xd, s_mm), (cd, s_mm), (yd, s_out)):
-            t.record_stream(s)
-        keep.append((xd, cd, yd))
-    for s in (s_in, s_mm, s_out):
-        main.wait_stream(s)
-    return out
+        out = torch.empty(input.size(0), weights.size(1), dtype=input.dtype,
+                          pin_memory=True)
+    return _C.grouped_gemm_host(input.contiguous(), weights.contiguous(),
+                                tokens_per_expert, out, int(tile_config), sort_by_m, chunks)
