@@ -169,7 +169,15 @@ int env_int(const char* name, int dflt) {
   const int v = e ? atoi(e) : 0;
   return v > 0 ? v : dflt;
 }
-int raster_group_m() { return env_int("GGO_RASTER_GROUP_M", 8); }
+// m-tiles per raster group: as many as keep the group's A panels (tile_m x K bf16 each) within
+// ~48 MB of L2, at most 16. Inside a group every weight column is streamed from HBM once, so
+// taller groups re-read the weights less; beyond the L2 budget the A panels themselves thrash.
+int raster_group_m(int64_t k, int tile_m) {
+  const int64_t panel = static_cast<int64_t>(tile_m) * k * 2;
+  int64_t g = (48ll << 20) / (panel > 0 ? panel : 1);
+  g = g < 1 ? 1 : (g > 16 ? 16 : g);
+  return env_int("GGO_RASTER_GROUP_M", static_cast<int>(g));
+}
 
 int device_setup(int* dev_out) {
   int dev;
@@ -258,7 +266,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.n_b = static_cast<int>(swiglu ? 2 * n : n);
   p.k = static_cast<int>(k);
   p.sort_by_m = sort_by_m ? 1 : 0;
-  p.group_m = raster_group_m();
+  p.group_m = raster_group_m(k, 128);  // re-derived below for 256-row pair tiles
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.origin = scatter ? ex->origin : nullptr;
   for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;
@@ -267,6 +275,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
   if (bn == 512) {
+    p.group_m = raster_group_m(k, 256);
     const int pbn = env_int("GGO_PAIR_BN", kDefaultPairBN);
     if (swiglu)
       return bf16 ? launch_pair_bn<kEpiSwiGLU, true>(pbn, input, weights, b_rows, p, dev, stream)
