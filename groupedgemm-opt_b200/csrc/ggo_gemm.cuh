@@ -76,6 +76,8 @@ struct GemmParams {
   const int32_t* origin;
   void* peer_out[8];
   int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
+  long long wait_limit;   // bounded-wait limit in SM cycles
+  int inject_stall;       // test hook: CTA 0 never arms its first pipeline stage
   GgoWorkspace* ws;
 };
 
@@ -201,6 +203,22 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
 // Maps flat tile index t (< total tiles) to its rows, output columns and weight rows.
 // Tiles of one segment are rastered in groups of p.group_m m-tiles: inside a group the m index
 // runs fastest, so concurrently running CTAs share the weight tile in L2.
+// After an abort, waits (bounded by `limit` cycles per stage) for the bulk loads this producer
+// issued into stages the MMA never consumed, so no copy is still landing in shared memory when the
+// CTA exits. Stage s was last armed with phase parity bit s of `armed_par`.
+template <int S>
+__device__ __forceinline__ void drain_armed_stages(uint64_t* full_bar, uint32_t armed,
+                                                   uint32_t armed_par, long long limit) {
+  for (int s = 0; s < S; ++s) {
+    if (!(armed >> s & 1u)) continue;
+    const uint32_t a = smem_u32(&full_bar[s]);
+    const uint32_t par = armed_par >> s & 1u;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(a, par) && clock64() - t0 < limit) {
+    }
+  }
+}
+
 template <int TILE_M, int OUT_BN, int EPI, int B_HALF>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* t_cnt,
                                                 const int* t_rowoff, const int* t_order,
@@ -374,8 +392,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* sche_bar = schf_bar + kSchedDepth;
   TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
+  int* total_tiles_s = reinterpret_cast<int*>(tmem_slot + 1);
+  WaitGuard* guard = reinterpret_cast<WaitGuard*>(tmem_slot + 4);  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -395,7 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&schf_bar[i], 1);
       mbar_init(&sche_bar[i], 1 + 4);
     }
-    *abort_flag = 0;
+    guard->abort = 0;
+    guard->limit = p.wait_limit;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -417,32 +436,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- TMA producer
     if (lane == 0) {
       int stage = 0, phase = 0, q = 0, qphase = 0;
+      uint32_t armed = 0, armed_par = 0;  // stages whose loads were issued, and their parity
+      bool first_tile = true;
       while (true) {
         const int t = atomicAdd(&p.ws->tile_counter, 1);
         TileInfo info;
         info.rows = 0;
         if (t < total_tiles) info = decode_tile<kBM, kOutBN, EPI, 128>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
-        if (!mbar_wait(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
+        if (!mbar_wait(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (info.rows == 0) break;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, err, kDevTimeoutProducer)) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, guard, err, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = tiles + stage * L::kStageBytes;
-          uint8_t* b_dst = a_dst + L::kABytes;
-          mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
-          tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, info.row0);
-          tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
-          if (BN == 256) tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+          // test hook: CTA 0 leaves its first stage unarmed, so the MMA's bounded wait expires
+          const bool skip = p.inject_stall && blockIdx.x == 0 && first_tile && kb == 0;
+          if (!skip) {
+            uint8_t* a_dst = tiles + stage * L::kStageBytes;
+            uint8_t* b_dst = a_dst + L::kABytes;
+            mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, info.row0);
+            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
+            if (BN == 256)
+              tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+            armed |= 1u << stage;
+            armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
+          }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
+        first_tile = false;
         if (!ok) break;
       }
+      if (guard->abort) drain_armed_stages<S>(full_bar, armed, armed_par, guard->limit);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
@@ -451,17 +481,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
-        if (!mbar_wait(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutMma)) break;
+        if (!mbar_wait(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
         const bool valid = ring[q].rows > 0;
         mbar_arrive(&sche_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (!valid) break;
-        if (!mbar_wait(&acce_bar[acc], aphase ^ 1, abort_flag, err, kDevTimeoutMma)) break;
+        if (!mbar_wait(&acce_bar[acc], aphase ^ 1, guard, err, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, err, kDevTimeoutMma)) {
+          if (!mbar_wait(&full_bar[stage], phase, guard, err, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -487,13 +517,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 4;  // TMEM lane quarter this warp may access
     int q = 0, qphase = 0, acc = 0, aphase = 0;
     while (true) {
-      if (!mbar_wait(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait(&schf_bar[q], qphase, guard, err, kDevTimeoutEpilogue)) break;
       const TileInfo info = ring[q];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sche_bar[q]);
       if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
       if (info.rows == 0) break;
-      if (!mbar_wait(&accf_bar[acc], aphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait(&accf_bar[acc], aphase, guard, err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const int r_local = ew * 32 + lane;
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;

@@ -69,8 +69,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint64_t* sche_bar = schf_bar + kSchedDepth;
   TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* total_tiles_s = const_cast<int*>(abort_flag) + 1;
+  int* total_tiles_s = reinterpret_cast<int*>(tmem_slot + 1);
+  WaitGuard* guard = reinterpret_cast<WaitGuard*>(tmem_slot + 4);  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -91,7 +91,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&schf_bar[i], 1);              // both: the leader producer
       mbar_init(&sche_bar[i], 1 + 4 + 1 + 4);  // leader: MMA, 4+4 epilogue warps, peer producer
     }
-    *abort_flag = 0;
+    guard->abort = 0;
+    guard->limit = p.wait_limit;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -114,6 +115,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- TMA producers (both CTAs)
     if (lane == 0) {
       int stage = 0, phase = 0, q = 0, qphase = 0;
+      uint32_t armed = 0, armed_par = 0;  // leader: stages armed, and their parity
+      bool first_tile = true;
       while (true) {
         TileInfo info;
         if (leader) {
@@ -121,7 +124,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           info.rows = 0;
           if (t < total_tiles)
             info = decode_tile<kTileM, kOutBN, EPI, BN / 2>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
-          if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, abort_flag, err, kDevTimeoutProducer))
+          if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer))
             break;
           ring[q] = info;
           const uint32_t pr = mapa_shared(&ring[q], 1);
@@ -130,7 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           mbar_arrive(&schf_bar[q]);
           mbar_arrive_cluster(mapa_shared(&schf_bar[q], 1));
         } else {
-          if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutProducer))
+          if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutProducer))
             break;
           info = ring[q];
           mbar_arrive_cluster(mapa_shared(&sche_bar[q], 0));
@@ -141,21 +144,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int b_row = leader ? info.brow0 : info.brow1;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, abort_flag, err,
+          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1, guard, err,
                                  kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = tiles + stage * L::kStageBytes;
-          uint8_t* b_dst = a_dst + L::kABytes;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
-          const uint32_t fb = mapa_shared(&full_bar[stage], 0);
-          tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, a_row);
-          tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+          // test hook: the first pair's leader leaves its first stage unarmed
+          const bool skip =
+              p.inject_stall && blockIdx.x == 0 && leader && first_tile && kb == 0;
+          if (!skip) {
+            uint8_t* a_dst = tiles + stage * L::kStageBytes;
+            uint8_t* b_dst = a_dst + L::kABytes;
+            if (leader) {
+              mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+              armed |= 1u << stage;
+              armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
+            }
+            const uint32_t fb = mapa_shared(&full_bar[stage], 0);
+            tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, a_row);
+            tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+          }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
+        first_tile = false;
         if (!ok) break;
       }
+      // the leader's barriers count both CTAs' bytes; the final cluster barrier keeps the peer
+      // resident until this drain is over
+      if (leader && guard->abort) drain_armed_stages<S>(full_bar, armed, armed_par, guard->limit);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer (leader only)
@@ -164,17 +180,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
-        if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutMma)) break;
+        if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
         const bool valid = ring[q].rows > 0;
         mbar_arrive(&sche_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (!valid) break;
-        if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, abort_flag, err, kDevTimeoutMma)) break;
+        if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, guard, err, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccStride;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_cluster(&full_bar[stage], phase, abort_flag, err, kDevTimeoutMma)) {
+          if (!mbar_wait_cluster(&full_bar[stage], phase, guard, err, kDevTimeoutMma)) {
             ok = false;
             break;
           }
@@ -199,13 +215,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int q = 0, qphase = 0, acc = 0, aphase = 0;
     using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     while (true) {
-      if (!mbar_wait_cluster(&schf_bar[q], qphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutEpilogue)) break;
       const TileInfo info = ring[q];
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&sche_bar[q], 0));
       if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
       if (info.rows == 0) break;
-      if (!mbar_wait_cluster(&accf_bar[acc], aphase, abort_flag, err, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait_cluster(&accf_bar[acc], aphase, guard, err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const int r_local = static_cast<int>(rank) * 128 + ew * 32 + lane;
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;

@@ -18,6 +18,14 @@
 
 namespace ggo {
 
+// Per-CTA wait state in shared memory: the abort flag every bounded wait polls, and the limit
+// (SM clock cycles) after which a wait gives up.
+struct WaitGuard {
+  volatile int abort;
+  int pad;
+  long long limit;
+};
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -56,16 +64,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 
 // Bounded wait on `bar` completing the phase with parity `parity`.
 // Returns false when the CTA aborted (limit hit here or elsewhere in the CTA).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, WaitGuard* g, int* err,
+                                          int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > GGO_WAIT_LIMIT_CYCLES) {
-      *abort_flag = 1;
+    if (g->abort) return false;
+    if (clock64() - t0 > g->limit) {
+      g->abort = 1;
       atomicCAS(err, 0, code);
       return false;
     }
@@ -238,16 +246,16 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t pa
   return ok != 0;
 }
 // Bounded wait with cluster-scope acquire (for barriers arrived on from the peer CTA).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort_flag, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, WaitGuard* g,
+                                                  int* err, int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait_cluster(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait_cluster(a, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > GGO_WAIT_LIMIT_CYCLES) {
-      *abort_flag = 1;
+    if (g->abort) return false;
+    if (clock64() - t0 > g->limit) {
+      g->abort = 1;
       atomicCAS(err, 0, code);
       return false;
     }

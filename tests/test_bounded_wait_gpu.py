@@ -1,0 +1,35 @@
+"""Failure detection on the GPU without a fault: a test hook (GGO_TEST_INJECT_STALL) makes the
+first CTA leave one pipeline stage unarmed and lowers the bounded-wait limit to ~10 ms. The kernel
+must return on its own, record a timeout in the workspace (read back as RuntimeError by
+check_device_errors) and leave the context usable: the next normal call is correct."""
+import time
+
+import pytest
+import torch
+
+import grouped_gemm_oracle as oracle
+from gpu_util import assert_parity
+from inputs import gemm_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.mark.parametrize("tc", [1, 3])  # single-CTA 128x256 kernel, CTA-pair kernel
+def test_bounded_wait_times_out_and_recovers(tc, monkeypatch):
+    import grouped_gemm_opt as ggo
+    x, w, tpe = gemm_inputs([700, 300, 1100, 20], 512, 1024, seed=tc)
+    xd, wd, td = x.to(DEV), w.to(DEV), tpe.to(DEV)
+    ggo.check_device_errors(0)
+    monkeypatch.setenv("GGO_TEST_INJECT_STALL", "1")
+    t0 = time.time()
+    ggo.grouped_gemm_opt(xd, wd, td, tc)
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 30.0
+    with pytest.raises(RuntimeError, match="error code 10[1-3]"):
+        ggo.check_device_errors(0)
+    monkeypatch.delenv("GGO_TEST_INJECT_STALL")
+    out = ggo.grouped_gemm_opt(xd, wd, td, tc)
+    torch.cuda.synchronize()
+    ggo.check_device_errors(0)
+    assert_parity(out, oracle.sequential_gemm(x, w, tpe), f"after timeout tc={tc}")
