@@ -26,7 +26,7 @@ def test_bounded_wait_times_out_and_recovers(tc, monkeypatch):
     ggo.grouped_gemm_opt(xd, wd, td, tc)
     torch.cuda.synchronize()
     assert time.time() - t0 < 30.0
-    with pytest.raises(RuntimeError, match="error code 10[1-3]"):
+    with pytest.raises(RuntimeError, match="error code 8$"):  # GGO_ERR_DEVICE_TIMEOUT
         ggo.check_device_errors(0)
     monkeypatch.delenv("GGO_TEST_INJECT_STALL")
     out = ggo.grouped_gemm_opt(xd, wd, td, tc)
