@@ -101,15 +101,24 @@ int kernel_setup(Kern kern, int smem, int dev, bool pair, int* resident) {
   return GGO_OK;
 }
 
-template <int BN, int EPI, bool BF16>
+// Weight map: K-major rows of K (boxes of 64 x box_rows), or for an MN-major operand
+// (the dgrad form) [E * Kred rows, n_out columns] in 64 x 64 boxes.
+template <bool BMN>
+int make_b_map(CUtensorMap* m, const void* b, int64_t b_rows, const GemmParams& q, bool bf16,
+               int box_rows) {
+  if (BMN) return make_map(m, b, static_cast<int64_t>(q.num_experts) * q.k, q.n_out, bf16, 64, 64);
+  return make_map(m, b, b_rows, q.k, bf16, box_rows);
+}
+
+template <int BN, int EPI, bool BF16, bool BMN = false>
 int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
            cudaStream_t stream) {
   CUtensorMap ma, mb, mc;
   GemmParams q = p;
   if (int st = make_map(&ma, a, q.rows, q.k, BF16, kBM)) return st;
-  if (int st = make_map(&mb, b, b_rows, q.k, BF16, 128)) return st;
+  if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, 128)) return st;
   if (int st = make_out_map(&mc, &q, BF16)) return st;
-  auto kern = grouped_gemm_kernel<BN, EPI, BF16>;
+  auto kern = grouped_gemm_kernel<BN, EPI, BF16, BMN>;
   constexpr int smem = SmemLayout<BN>::kTotal;
   int sms = 0;
   if (int st = kernel_setup(kern, smem, dev, false, &sms)) return st;
@@ -122,15 +131,15 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
 }
 
-template <int BN, int EPI, bool BF16>
+template <int BN, int EPI, bool BF16, bool BMN = false>
 int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
                 cudaStream_t stream) {
   CUtensorMap ma, mb, mc;
   GemmParams q = p;
   if (int st = make_map(&ma, a, q.rows, q.k, BF16, 128)) return st;
-  if (int st = make_map(&mb, b, b_rows, q.k, BF16, BN / 2)) return st;
+  if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, BN / 2)) return st;
   if (int st = make_out_map(&mc, &q, BF16)) return st;
-  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16>;
+  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16, BMN>;
   constexpr int smem = PairLayout<BN>::kTotal;
   int clusters = 0;
   if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
@@ -231,7 +240,7 @@ struct GemmExtras {
 int gemm_common(const void* input, const void* weights, void* output, const int64_t* counts,
                 int num_segments, int num_experts, int64_t rows, int64_t n, int64_t k, int dtype,
                 int tile_config, int sort_by_m, void* workspace, cudaStream_t stream, bool swiglu,
-                const GemmExtras* ex = nullptr) {
+                const GemmExtras* ex = nullptr, bool bmn = false) {
   const bool scatter = ex && ex->origin;
   if (!input || !weights || (!output && !scatter) || !counts || !workspace)
     return GGO_ERR_INVALID_ARG;
@@ -253,6 +262,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
     return GGO_ERR_ALIGNMENT;
   const int64_t b_rows = static_cast<int64_t>(num_experts) * (swiglu ? 2 * n : n);
   if (rows > INT32_MAX || b_rows > INT32_MAX || k > INT32_MAX) return GGO_ERR_SHAPE;
+  if (bmn && static_cast<int64_t>(num_experts) * k > INT32_MAX) return GGO_ERR_SHAPE;
   if (rows == 0) return GGO_OK;
   int dev;
   if (int st = device_setup(&dev)) return st;
@@ -279,6 +289,18 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
+  if (bmn) {  // dgrad form: MN-major weights, plain epilogue
+    if (bn == 512) {
+      p.group_m = raster_group_m(k, 256);
+      return bf16 ? launch_pair<256, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
+                  : launch_pair<256, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
+    }
+    if (bn == 256)
+      return bf16 ? launch<256, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
+                  : launch<256, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
+    return bf16 ? launch<128, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
+                : launch<128, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
+  }
   if (bn == 512) {
     p.group_m = raster_group_m(k, 256);
     const int pbn = env_int("GGO_PAIR_BN", kDefaultPairBN);
@@ -389,6 +411,16 @@ int ggo_grouped_gemm_noalloc(const void* input_dev, const void* weights_dev, voi
   return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_expert_dev, num_experts,
                           num_experts, total_tokens, N, K, dtype, tile_config, sort_by_m, scratch,
                           stream, false);
+}
+
+int ggo_grouped_gemm_dgrad(const void* dy_dev, const void* weights_dev, void* dx_dev,
+                           const int64_t* tokens_per_expert_dev, int num_experts,
+                           int64_t total_tokens, int64_t N, int64_t K, int dtype, int tile_config,
+                           int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  // dx [T, K] = dy [T, N] @ W[e]: reduction over N, output width K, weights read MN-major
+  return ggo::gemm_common(dy_dev, weights_dev, dx_dev, tokens_per_expert_dev, num_experts,
+                          num_experts, total_tokens, K, N, dtype, tile_config, sort_by_m,
+                          workspace_dev, stream, false, nullptr, true);
 }
 
 int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,

@@ -219,7 +219,7 @@ __device__ __forceinline__ void drain_armed_stages(uint64_t* full_bar, uint32_t 
   }
 }
 
-template <int TILE_M, int OUT_BN, int EPI, int B_HALF>
+template <int TILE_M, int OUT_BN, int EPI, int B_HALF, bool BMN = false>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* t_cnt,
                                                 const int* t_rowoff, const int* t_order,
                                                 const int* t_tileoff) {
@@ -246,7 +246,11 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
   info.rows = min(TILE_M, t_cnt[seg] - m_idx * TILE_M);
   info.seg = seg;
   info.n0 = n_idx * OUT_BN;
-  if (EPI == kEpiSwiGLU) {
+  if (BMN) {
+    // MN-major weights [E, Kred, n_out]: rows are the reduction index; the column is n0
+    info.brow0 = expert * p.k;
+    info.brow1 = info.brow0;
+  } else if (EPI == kEpiSwiGLU) {
     info.brow0 = expert * p.n_b + info.n0;                 // gate rows
     info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
   } else {
@@ -363,7 +367,7 @@ __device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo&
   return reinterpret_cast<OutT*>(p.peer_out[src]) + static_cast<size_t>(p.origin[r]) * p.n_out;
 }
 
-template <int BN, int EPI, bool BF16>
+template <int BN, int EPI, bool BF16, bool BMN = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -442,7 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = atomicAdd(&p.ws->tile_counter, 1);
         TileInfo info;
         info.rows = 0;
-        if (t < total_tiles) info = decode_tile<kBM, kOutBN, EPI, 128>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+        if (t < total_tiles)
+          info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);
@@ -461,9 +466,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* b_dst = a_dst + L::kABytes;
             mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
             tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, info.row0);
-            tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
-            if (BN == 256)
-              tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+            if (BMN) {  // BN/64 boxes of [64 reduction rows][64 output columns]
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i)
+                tma_load_2d(b_dst + i * 8192, &tmB, &full_bar[stage], info.n0 + 64 * i,
+                            info.brow0 + kb * kBK);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
+              if (BN == 256)
+                tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+            }
             armed |= 1u << stage;
             armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
           }
@@ -477,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kBM, BN, BF16);
+      constexpr uint32_t idesc = idesc_f16(kBM, BN, BF16, BMN);
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
@@ -498,12 +510,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = tiles_addr + stage * L::kStageBytes;
           const uint64_t adesc = sdesc_sw128_kmajor(a_addr);
-          const uint64_t bdesc = sdesc_sw128_kmajor(a_addr + L::kABytes);
+          const uint64_t bdesc = BMN ? sdesc_sw128_mnmajor(a_addr + L::kABytes, 8192)
+                                     : sdesc_sw128_kmajor(a_addr + L::kABytes);
+          // per 16-element K step: A (K-major) advances 32 B inside its swizzle atom; a K-major
+          // B likewise, an MN-major B by 16 rows of 128 B (two 8-row atoms)
+          constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-            // advance 16 elements (32 B) along K inside the 128-B swizzle atom
-            mma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            mma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
           mma_commit(&empty_bar[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }

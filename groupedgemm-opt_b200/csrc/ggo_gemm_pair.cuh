@@ -36,7 +36,7 @@ struct PairLayout {
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, int EPI, bool BF16>
+template <int BN, int EPI, bool BF16, bool BMN = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
@@ -123,7 +123,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int t = atomicAdd(&p.ws->tile_counter, 1);
           info.rows = 0;
           if (t < total_tiles)
-            info = decode_tile<kTileM, kOutBN, EPI, BN / 2>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+            info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(t, p, t_cnt, t_rowoff, t_order,
+                                                               t_tileoff);
           if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer))
             break;
           ring[q] = info;
@@ -162,7 +163,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t fb = mapa_shared(&full_bar[stage], 0);
             tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, a_row);
-            tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+            if (BMN) {  // this CTA's BN/2 output columns as 64-column boxes
+#pragma unroll
+              for (int i = 0; i < BN / 128; ++i)
+                tma_load_2d_pair(b_dst + i * 8192, &tmB, fb,
+                                 info.n0 + static_cast<int>(rank) * (BN / 2) + 64 * i,
+                                 info.brow0 + kb * kBK);
+            } else {
+              tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+            }
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -176,7 +185,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer (leader only)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kTileM, BN, BF16);
+      constexpr uint32_t idesc = idesc_f16(kTileM, BN, BF16, BMN);
+      static_assert(!BMN || (BN / 2) % 64 == 0, "MN-major B halves are whole 64-column boxes");
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
@@ -197,10 +207,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = tiles_addr + stage * L::kStageBytes;
           const uint64_t adesc = sdesc_sw128_kmajor(a_addr);
-          const uint64_t bdesc = sdesc_sw128_kmajor(a_addr + L::kABytes);
+          const uint64_t bdesc = BMN ? sdesc_sw128_mnmajor(a_addr + L::kABytes, 8192)
+                                     : sdesc_sw128_kmajor(a_addr + L::kABytes);
+          constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
 #pragma unroll
           for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-            mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+            mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
           mma_commit_pair(&empty_bar[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }

@@ -203,9 +203,25 @@ __device__ __forceinline__ uint64_t sdesc_sw128_kmajor(uint32_t saddr) {
 // Instruction descriptor for tcgen05.mma kind::f16, dense, fp32 accumulator, both operands K-major.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16),
 //   bits 17-22 N >> 3, bits 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16) {
+//   bit 16: B major (0 = K-major, 1 = MN-major).
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool bf16, bool b_mn_major = false) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Shared-memory descriptor for an MN-major operand stored as TMA writes 64 x 64 boxes with the
+// 128-byte swizzle: each 128-B row holds 64 consecutive MN elements of one K index, 8 K rows form
+// a 1024-B swizzle atom (SBO = 1024 B between K groups) and consecutive 64-element MN groups are
+// whole boxes, `mn_stride` bytes apart (LBO).
+__device__ __forceinline__ uint64_t sdesc_sw128_mnmajor(uint32_t saddr, uint32_t mn_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
 }
 
 // ---------------------------------------------------------------- clusters (CTA pairs)

@@ -100,6 +100,32 @@ torch::Tensor grouped_gemm_forward(const torch::Tensor& input, const torch::Tens
                                sort_by_m);
 }
 
+// dx = dy @ W[e] per expert segment (weights [E, N, K], dy [T, N] -> dx [T, K]).
+torch::Tensor grouped_gemm_dgrad(const torch::Tensor& dy, const torch::Tensor& weights,
+                                 const torch::Tensor& tokens_per_expert, int64_t tile_config,
+                                 bool sort_by_m) {
+  TORCH_CHECK(dy.is_cuda() && weights.is_cuda(), "dy and weights must be on CUDA");
+  TORCH_CHECK(dy.dim() == 2 && weights.dim() == 3, "dy [T, N], weights [E, N, K]");
+  TORCH_CHECK(dy.size(1) == weights.size(1), "N mismatch: dy=", dy.size(1), " vs weights=",
+              weights.size(1));
+  TORCH_CHECK(dy.is_contiguous() && weights.is_contiguous(), "dy and weights must be contiguous");
+  TORCH_CHECK(dy.scalar_type() == weights.scalar_type(), "dy/weights dtype mismatch");
+  TORCH_CHECK(tokens_per_expert.dim() == 1 && tokens_per_expert.size(0) == weights.size(0),
+              "tokens_per_expert must be 1D with num_experts entries");
+  c10::cuda::CUDAGuard guard(dy.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = dy.size(0), N = weights.size(1), K = weights.size(2);
+  auto dx = torch::empty({T, K}, dy.options());
+  if (T == 0) return dx;
+  auto c = counts_on_device(tokens_per_expert, dy.device());
+  const int st = ggo_grouped_gemm_dgrad(
+      dy.data_ptr(), weights.data_ptr(), dx.data_ptr(), c.data_ptr<int64_t>(),
+      static_cast<int>(weights.size(0)), T, N, K, dtype_code(dy), static_cast<int>(tile_config),
+      sort_by_m ? 1 : 0, workspace_for(dy.device(), stream), stream);
+  check_status(st, "grouped GEMM dgrad");
+  return dx;
+}
+
 torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
                                   const torch::Tensor& counts, int64_t num_experts,
                                   bool sort_by_m) {
@@ -399,6 +425,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_segments", &grouped_gemm_segments, py::arg("input"), py::arg("weights"),
         py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("tile_config") = 4,
         py::arg("sort_by_m") = true);
+  m.def("grouped_gemm_dgrad", &grouped_gemm_dgrad, py::arg("dy"), py::arg("weights"),
+        py::arg("tokens_per_expert"), py::arg("tile_config") = 4, py::arg("sort_by_m") = true);
   m.def("grouped_gemm_swiglu", &grouped_gemm_swiglu, py::arg("x"), py::arg("w_gate_up"),
         py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("sort_by_m") = true);
   m.def("moe_route", &moe_route, py::arg("router_logits"), py::arg("top_k"));

@@ -100,6 +100,16 @@ int ggo_grouped_gemm_segments(const void* input_dev, const void* weights_dev, vo
                               int dtype, int tile_config, int sort_by_m, void* workspace_dev,
                               cudaStream_t stream);
 
+/* Backward, input gradient of the grouped GEMM (no reference counterpart: the reference is
+ * forward-only):
+ *   dx[r, :] = dy[r, :] @ weights[e(r)]        dy [T, N], weights [E, N, K], dx [T, K]
+ * The weights are read in place (MN-major operand), no transposed copy. Same segment, count and
+ * alignment rules as ggo_grouped_gemm; tile_config as there. */
+int ggo_grouped_gemm_dgrad(const void* dy_dev, const void* weights_dev, void* dx_dev,
+                           const int64_t* tokens_per_expert_dev, int num_experts,
+                           int64_t total_tokens, int64_t N, int64_t K, int dtype, int tile_config,
+                           int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
 /* Fused-MoE stage 2: gate/up grouped GEMM with the SwiGLU epilogue.
  *   h[r, f] = silu(x[r,:] . Wgu[e, f, :]) * (x[r,:] . Wgu[e, F + f, :])
  * w_gate_up_dev [num_experts, 2F, K]: rows 0..F-1 gate, rows F..2F-1 up.

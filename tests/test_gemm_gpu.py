@@ -236,3 +236,21 @@ def test_host_buffer_api(ggo, chunks):
     torch.cuda.synchronize()
     assert not out.is_cuda
     assert_parity(out, ref, f"host api chunks={chunks}")
+
+
+@pytest.mark.parametrize("tc", [0, 1, 3, 4])
+@pytest.mark.parametrize("counts,n,k", [([300, 0, 17, 513, 256], 256, 384),
+                                        ([1, 7, 8, 127, 128, 129], 200, 1000),
+                                        ([4000, 3000], 512, 2048)])
+def test_dgrad(tc, counts, n, k):
+    """dx = dy @ W[e] per segment (weights read MN-major in place)."""
+    from grouped_gemm_opt import _C
+    g = torch.Generator().manual_seed(len(counts) + tc)
+    tpe = torch.tensor(counts)
+    dy = torch.randn(int(tpe.sum()), n, generator=g).to(torch.bfloat16)
+    w = (torch.randn(len(counts), n, k, generator=g) * 0.05).to(torch.bfloat16)
+    wt = w.transpose(1, 2).contiguous()  # [E, K, N]: dgrad is a forward GEMM with W^T
+    ref = oracle.sequential_gemm(dy, wt, tpe)
+    dx = _C.grouped_gemm_dgrad(dy.to(DEV), w.to(DEV), tpe.to(DEV), tc, True)
+    assert dx.shape == (dy.size(0), k)
+    assert_parity(dx, ref, f"dgrad tc={tc} n={n} k={k}")
