@@ -25,7 +25,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 
 CU_SOURCES = ["ggo_gemm.cu", "ggo_moe.cu"]
-CU_HEADERS = ["ggo_gemm.cuh", "ggo_gemm_pair.cuh", "ggo_ptx.cuh", "ggo_internal.h"]
+CU_HEADERS = ["ggo_gemm.cuh", "ggo_gemm_pair.cuh", "ggo_gemm_wgrad.cuh", "ggo_ptx.cuh", "ggo_internal.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB_NAME = "libggo_b200.so"
 

@@ -13,6 +13,7 @@
 #include "ggo.h"
 #include "ggo_gemm.cuh"
 #include "ggo_gemm_pair.cuh"
+#include "ggo_gemm_wgrad.cuh"
 #include "ggo_internal.h"
 
 namespace ggo {
@@ -320,6 +321,59 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
               : launch<128, kEpiStore, false>(input, weights, b_rows, p, dev, stream);
 }
 
+template <int BN, bool BF16>
+int launch_wgrad(const void* x, const void* dy, void* dw, const WgradParams& p, int dev,
+                 cudaStream_t stream) {
+  CUtensorMap mdy, mx, mw;
+  if (int st = make_map(&mdy, dy, p.rows, p.n, BF16, 64, 64)) return st;
+  if (int st = make_map(&mx, x, p.rows, p.k, BF16, 64, 64)) return st;
+  if (int st = make_map(&mw, dw, static_cast<int64_t>(p.num_experts) * p.n, p.k, BF16, 32, 64))
+    return st;
+  auto kern = grouped_gemm_wgrad_kernel<BN, BF16>;
+  constexpr int smem = WgradLayout<BN>::kTotal;
+  int sms = 0;
+  if (int st = kernel_setup(kern, smem, dev, false, &sms)) return st;
+  const int64_t tiles = static_cast<int64_t>(p.num_experts) * ((p.n + 127) / 128) *
+                        ((p.k + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  kern<<<grid, kThreads, smem, stream>>>(mdy, mx, mw, p);
+  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+}
+
+int wgrad_common(const void* x, const void* dy, void* dw, const int64_t* counts, int num_experts,
+                 int64_t rows, int64_t n, int64_t k, int dtype, int sort_by_m, void* workspace,
+                 cudaStream_t stream) {
+  if (!x || !dy || !dw || !counts || !workspace) return GGO_ERR_INVALID_ARG;
+  if (num_experts <= 0 || rows < 0 || n <= 0 || k <= 0) return GGO_ERR_INVALID_ARG;
+  if (num_experts > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
+  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
+  if ((k % 8) || (n % 8)) return GGO_ERR_ALIGNMENT;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw)) return GGO_ERR_ALIGNMENT;
+  if (rows > INT32_MAX || n > INT32_MAX || k > INT32_MAX ||
+      static_cast<int64_t>(num_experts) * n > INT32_MAX)
+    return GGO_ERR_SHAPE;
+  int dev;
+  if (int st = device_setup(&dev)) return st;
+  WgradParams p;
+  p.counts = counts;
+  p.num_experts = num_experts;
+  p.rows = static_cast<int>(rows);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.sort_by_m = sort_by_m ? 1 : 0;
+  p.out = dw;
+  p.ws = static_cast<GgoWorkspace*>(workspace);
+  p.wait_limit = GGO_WAIT_LIMIT_CYCLES;
+  // 128x256 tiles unless they leave SMs idle
+  const int64_t wide = static_cast<int64_t>(num_experts) * ((n + 127) / 128) * ((k + 255) / 256);
+  const bool bf16 = dtype == GGO_DTYPE_BF16;
+  if (wide >= g_sm_count[dev])
+    return bf16 ? launch_wgrad<256, true>(x, dy, dw, p, dev, stream)
+                : launch_wgrad<256, false>(x, dy, dw, p, dev, stream);
+  return bf16 ? launch_wgrad<128, true>(x, dy, dw, p, dev, stream)
+              : launch_wgrad<128, false>(x, dy, dw, p, dev, stream);
+}
+
 }  // namespace
 
 // Scratch for ggo_grouped_gemm_noalloc: one workspace (tile counter, done counter, error word) in
@@ -421,6 +475,14 @@ int ggo_grouped_gemm_dgrad(const void* dy_dev, const void* weights_dev, void* dx
   return ggo::gemm_common(dy_dev, weights_dev, dx_dev, tokens_per_expert_dev, num_experts,
                           num_experts, total_tokens, K, N, dtype, tile_config, sort_by_m,
                           workspace_dev, stream, false, nullptr, true);
+}
+
+int ggo_grouped_gemm_wgrad(const void* x_dev, const void* dy_dev, void* dw_dev,
+                           const int64_t* tokens_per_expert_dev, int num_experts,
+                           int64_t total_tokens, int64_t N, int64_t K, int dtype, int sort_by_m,
+                           void* workspace_dev, cudaStream_t stream) {
+  return ggo::wgrad_common(x_dev, dy_dev, dw_dev, tokens_per_expert_dev, num_experts,
+                           total_tokens, N, K, dtype, sort_by_m, workspace_dev, stream);
 }
 
 int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,

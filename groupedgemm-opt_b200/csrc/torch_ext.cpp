@@ -126,6 +126,28 @@ torch::Tensor grouped_gemm_dgrad(const torch::Tensor& dy, const torch::Tensor& w
   return dx;
 }
 
+// dw[e] = dy_e^T @ x_e per expert (x [T, K], dy [T, N] -> dw [E, N, K]).
+torch::Tensor grouped_gemm_wgrad(const torch::Tensor& x, const torch::Tensor& dy,
+                                 const torch::Tensor& tokens_per_expert, bool sort_by_m) {
+  TORCH_CHECK(x.is_cuda() && dy.is_cuda(), "x and dy must be on CUDA");
+  TORCH_CHECK(x.dim() == 2 && dy.dim() == 2 && x.size(0) == dy.size(0),
+              "x [T, K] and dy [T, N] with the same rows");
+  TORCH_CHECK(x.is_contiguous() && dy.is_contiguous(), "x and dy must be contiguous");
+  TORCH_CHECK(x.scalar_type() == dy.scalar_type(), "x/dy dtype mismatch");
+  TORCH_CHECK(tokens_per_expert.dim() == 1, "tokens_per_expert must be 1D");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x.size(0), K = x.size(1), N = dy.size(1), E = tokens_per_expert.size(0);
+  auto dw = torch::empty({E, N, K}, x.options());
+  auto c = counts_on_device(tokens_per_expert, x.device());
+  const int st = ggo_grouped_gemm_wgrad(x.data_ptr(), dy.data_ptr(), dw.data_ptr(),
+                                        c.data_ptr<int64_t>(), static_cast<int>(E), T, N, K,
+                                        dtype_code(x), sort_by_m ? 1 : 0,
+                                        workspace_for(x.device(), stream), stream);
+  check_status(st, "grouped GEMM wgrad");
+  return dw;
+}
+
 torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
                                   const torch::Tensor& counts, int64_t num_experts,
                                   bool sort_by_m) {
@@ -427,6 +449,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sort_by_m") = true);
   m.def("grouped_gemm_dgrad", &grouped_gemm_dgrad, py::arg("dy"), py::arg("weights"),
         py::arg("tokens_per_expert"), py::arg("tile_config") = 4, py::arg("sort_by_m") = true);
+  m.def("grouped_gemm_wgrad", &grouped_gemm_wgrad, py::arg("x"), py::arg("dy"),
+        py::arg("tokens_per_expert"), py::arg("sort_by_m") = true);
   m.def("grouped_gemm_swiglu", &grouped_gemm_swiglu, py::arg("x"), py::arg("w_gate_up"),
         py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("sort_by_m") = true);
   m.def("moe_route", &moe_route, py::arg("router_logits"), py::arg("top_k"));

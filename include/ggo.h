@@ -110,6 +110,16 @@ int ggo_grouped_gemm_dgrad(const void* dy_dev, const void* weights_dev, void* dx
                            int64_t total_tokens, int64_t N, int64_t K, int dtype, int tile_config,
                            int sort_by_m, void* workspace_dev, cudaStream_t stream);
 
+/* Backward, weight gradient (no reference counterpart):
+ *   dw[e] = dy_e^T @ x_e        x [T, K], dy [T, N], dw [E, N, K]
+ * where x_e, dy_e are expert e's rows (segments given by tokens_per_expert, on the device). The
+ * reduction runs over each expert's own tokens; experts with no tokens get dw[e] = 0. Both
+ * operands are read in place. N and K multiples of 8. */
+int ggo_grouped_gemm_wgrad(const void* x_dev, const void* dy_dev, void* dw_dev,
+                           const int64_t* tokens_per_expert_dev, int num_experts,
+                           int64_t total_tokens, int64_t N, int64_t K, int dtype, int sort_by_m,
+                           void* workspace_dev, cudaStream_t stream);
+
 /* Fused-MoE stage 2: gate/up grouped GEMM with the SwiGLU epilogue.
  *   h[r, f] = silu(x[r,:] . Wgu[e, f, :]) * (x[r,:] . Wgu[e, F + f, :])
  * w_gate_up_dev [num_experts, 2F, K]: rows 0..F-1 gate, rows F..2F-1 up.

@@ -254,3 +254,34 @@ def test_dgrad(tc, counts, n, k):
     dx = _C.grouped_gemm_dgrad(dy.to(DEV), w.to(DEV), tpe.to(DEV), tc, True)
     assert dx.shape == (dy.size(0), k)
     assert_parity(dx, ref, f"dgrad tc={tc} n={n} k={k}")
+
+
+def _wgrad_ref(x, dy, tpe):
+    outs, off = [], 0
+    for m in tpe.tolist():
+        outs.append(dy[off:off + m].float().T @ x[off:off + m].float())
+        off += m
+    return torch.stack(outs)
+
+
+@pytest.mark.parametrize("sort", [False, True])
+@pytest.mark.parametrize("counts,n,k", [([300, 0, 17, 513, 256], 256, 384),
+                                        ([1, 7, 63, 64, 65, 130, 0], 200, 1000),
+                                        ([4000, 3000], 512, 2048),
+                                        ([0, 0, 5], 64, 64)])
+def test_wgrad(sort, counts, n, k):
+    """dw[e] = dy_e^T @ x_e over each expert's own tokens (zero for experts without tokens)."""
+    from grouped_gemm_opt import _C
+    g = torch.Generator().manual_seed(len(counts) * 7 + k)
+    tpe = torch.tensor(counts)
+    T = int(tpe.sum())
+    x = torch.randn(T, k, generator=g).to(torch.bfloat16)
+    dy = torch.randn(T, n, generator=g).to(torch.bfloat16)
+    ref = _wgrad_ref(x, dy, tpe)
+    dw = _C.grouped_gemm_wgrad(x.to(DEV), dy.to(DEV), tpe.to(DEV), sort)
+    assert dw.shape == (len(counts), n, k)
+    for e, m in enumerate(counts):
+        if m == 0:
+            assert (dw[e] == 0).all()
+        else:
+            assert_parity(dw[e], ref[e], f"wgrad expert {e} (m={m})")
