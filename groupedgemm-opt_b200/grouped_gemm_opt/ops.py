@@ -28,6 +28,30 @@ class TileConfig(IntEnum):
     CuBLAS_Seq = 5
 
 
+class _GroupedGemmFn(torch.autograd.Function):
+    """Autograd wrapper: forward = the tcgen05 grouped GEMM; backward = the dgrad kernel
+    (dx = dy @ W[e]) and the wgrad kernel (dW[e] = dy_e^T @ x_e). The reference is forward-only;
+    this makes the same call usable for training."""
+
+    @staticmethod
+    def forward(ctx, input, weights, tokens_per_expert, tile_config, sort_by_m):
+        ctx.save_for_backward(input, weights, tokens_per_expert)
+        ctx.tile_config, ctx.sort_by_m = tile_config, sort_by_m
+        return _C.grouped_gemm_opt_forward(input, weights, tokens_per_expert, tile_config,
+                                           sort_by_m)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        input, weights, tpe = ctx.saved_tensors
+        grad_out = grad_out.contiguous()
+        gi = gw = None
+        if ctx.needs_input_grad[0]:
+            gi = _C.grouped_gemm_dgrad(grad_out, weights, tpe, ctx.tile_config, ctx.sort_by_m)
+        if ctx.needs_input_grad[1]:
+            gw = _C.grouped_gemm_wgrad(input, grad_out, tpe, ctx.sort_by_m)
+        return gi, gw, None, None, None
+
+
 def grouped_gemm_opt(
     input: torch.Tensor,
     weights: torch.Tensor,
@@ -48,6 +72,9 @@ def grouped_gemm_opt(
     Returns:
         output: [total_tokens, N], same dtype as ``input``.
 
+    Differentiable: when ``input`` or ``weights`` requires grad, the backward runs the dgrad and
+    wgrad grouped-GEMM kernels.
+
     Raises AssertionError for non-CUDA operands, wrong ranks and (CPU counts only)
     ``sum(tokens_per_expert) != total_tokens`` -- as the reference (ops.py:57-64) -- and
     RuntimeError for dtype/shape/alignment errors (as the reference's TORCH_CHECKs).
@@ -62,6 +89,10 @@ def grouped_gemm_opt(
             f"sum(tokens_per_expert)={total} != total_tokens={input.size(0)}")
         # Zero-token experts need no host-side filtering (and no weight copy): the kernel skips
         # them while it builds its tile pool.
+    if torch.is_grad_enabled() and (input.requires_grad or weights.requires_grad):
+        return _GroupedGemmFn.apply(input.contiguous(), weights.contiguous(),
+                                    tokens_per_expert.to(input.device), int(tile_config),
+                                    sort_by_m)
     return _C.grouped_gemm_opt_forward(
         input.contiguous(),
         weights.contiguous(),
