@@ -6,6 +6,7 @@
 // cudaStreamSynchronize), zero-token experts are skipped inside the kernel, and there is no
 // per-group argument buffer to build or copy.
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -59,7 +60,7 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf1
                    const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? GGO_OK : GGO_ERR_CUDA;
+  return r == CUDA_SUCCESS ? GGO_OK : cuda_fail(100000 + static_cast<int>(r));
 }
 
 // Output map for the TMA-store epilogue: [rows, n_out] row-major, boxes of 32 rows x 64 columns
@@ -83,9 +84,9 @@ int kernel_setup(Kern kern, int smem, int dev, bool pair, int* resident) {
   auto key = std::make_pair(dev, reinterpret_cast<const void*>(kern));
   auto it = g_kernel_slots.find(key);
   if (it == g_kernel_slots.end()) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return GGO_ERR_CUDA;
+    if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem))
+      return cuda_fail(e);
     int n = g_sm_count[dev];
     if (pair) {
       cudaLaunchConfig_t cfg = {};
@@ -93,8 +94,8 @@ int kernel_setup(Kern kern, int smem, int dev, bool pair, int* resident) {
       cfg.blockDim = dim3(kThreads, 1, 1);
       cfg.dynamicSmemBytes = smem;
       n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
-        return GGO_ERR_CUDA;
+      if (cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg)) return cuda_fail(e);
+      if (n <= 0) return cuda_fail(static_cast<int>(cudaErrorInvalidConfiguration));
     }
     it = g_kernel_slots.emplace(key, n).first;
   }
@@ -129,7 +130,7 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   const int grid = static_cast<int>(ub < sms ? ub : sms);
   if (grid <= 0) return GGO_OK;
   kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, q);
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return check_launch();
 }
 
 template <int BN, int EPI, bool BF16, bool BMN = false>
@@ -150,7 +151,7 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
   const int64_t pairs = ub < clusters ? ub : clusters;
   if (pairs <= 0) return GGO_OK;
   kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, mc, q);
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return check_launch();
 }
 
 // Pair-tile width. 256 is the default: measured on cfg2 under the 1 kW power cap, 256-wide tiles
@@ -191,7 +192,8 @@ int raster_group_m(int64_t k, int tile_m) {
 
 int device_setup(int* dev_out) {
   int dev;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GGO_ERR_CUDA;
+  if (cudaError_t e = cudaGetDevice(&dev)) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return GGO_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_sm_count[dev] == 0) {
     int major = 0, sms = 0;
@@ -337,7 +339,7 @@ int launch_wgrad(const void* x, const void* dy, void* dw, const WgradParams& p, 
                         ((p.k + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   kern<<<grid, kThreads, smem, stream>>>(mdy, mx, mw, p);
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return check_launch();
 }
 
 int wgrad_common(const void* x, const void* dy, void* dw, const int64_t* counts, int num_experts,
@@ -530,6 +532,17 @@ int ggo_ipc_close(void* peer_ptr) {
 }
 
 int ggo_ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? GGO_OK : GGO_ERR_CUDA; }
+
+const char* ggo_last_cuda_error_string(void) {
+  const int c = ggo::g_last_cuda_error;
+  if (c == 0) return "no CUDA error recorded";
+  if (c >= 100000) {
+    static thread_local char buf[64];
+    snprintf(buf, sizeof(buf), "CUDA driver error %d", c - 100000);
+    return buf;
+  }
+  return cudaGetErrorString(static_cast<cudaError_t>(c));
+}
 
 int ggo_workspace_error(void* workspace_dev, cudaStream_t stream, int* status_out) {
   if (!workspace_dev || !status_out) return GGO_ERR_INVALID_ARG;

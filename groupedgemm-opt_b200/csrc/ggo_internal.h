@@ -3,7 +3,23 @@
 
 #include "ggo.h"
 
+#include <cuda_runtime_api.h>
+
 namespace ggo {
+
+// Last CUDA runtime error (or 100000 + driver CUresult) seen by a failing call on this thread,
+// reported by ggo_last_cuda_error_string().
+inline thread_local int g_last_cuda_error = 0;
+
+inline int cuda_fail(int code) {
+  g_last_cuda_error = code;
+  return GGO_ERR_CUDA;
+}
+
+inline int check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GGO_OK : cuda_fail(static_cast<int>(e));
+}
 
 // Maps a device-side error word (GgoWorkspace::error) to a public status code.
 inline int device_error_to_status(int code) {

@@ -13,6 +13,7 @@
 #include <cuda_fp16.h>
 
 #include "ggo.h"
+#include "ggo_internal.h"
 
 namespace ggo {
 namespace {
@@ -341,7 +342,7 @@ int dispatch_common(const void* x, int64_t num_tokens, int64_t hidden, int E, in
   else
     launch_dispatch<__half>(x, T, static_cast<int>(hidden), E, K, ids, bo, es, counts_all, world,
                             rank, recv, origin, stok, spos, stream);
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return ggo::check_launch();
 }
 
 }  // namespace
@@ -376,7 +377,7 @@ int ggo_moe_route(const float* logits_dev, int64_t num_tokens, int num_experts, 
         logits_dev, T, num_experts, top_k, topk_ids_dev, topk_weights_dev, bc);
   }
   ggo::route_scan_kernel<<<1, 1024, 0, stream>>>(bc, nb, num_experts, tokens_per_expert_dev);
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return ggo::check_launch();
 }
 
 int ggo_moe_permute(const void* x_dev, int64_t num_tokens, int64_t hidden, int num_experts,
@@ -428,7 +429,7 @@ int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
         static_cast<const __half*>(y_sorted_dev), topk_weights_dev, slot_pos_dev, T,
         static_cast<int>(hidden), top_k, static_cast<__half*>(out_dev));
   }
-  return cudaGetLastError() == cudaSuccess ? GGO_OK : GGO_ERR_CUDA;
+  return ggo::check_launch();
 }
 
 }  // extern "C"

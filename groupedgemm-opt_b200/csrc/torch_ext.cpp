@@ -22,7 +22,9 @@
 namespace {
 
 void check_status(int st, const char* what) {
-  TORCH_CHECK(st == GGO_OK, what, " failed: ", ggo_status_string(st), " (status ", st, ")");
+  TORCH_CHECK(st == GGO_OK, what, " failed: ", ggo_status_string(st), " (status ", st, ")",
+              st == GGO_ERR_CUDA ? std::string(": ") + ggo_last_cuda_error_string()
+                                 : std::string());
 }
 
 int dtype_code(const torch::Tensor& t) {

@@ -59,6 +59,9 @@ extern "C" {
 #define GGO_TILE_AUTO 4
 #define GGO_TILE_CUBLAS_SEQ 5
 
+/* After a call returned GGO_ERR_CUDA: the CUDA error it met, as text (this thread's last). */
+const char* ggo_last_cuda_error_string(void);
+
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int ggo_version(void);
 
