@@ -194,6 +194,9 @@ int device_setup(int* dev_out) {
   int dev;
   if (cudaError_t e = cudaGetDevice(&dev)) return cuda_fail(e);
   if (dev < 0 || dev >= kMaxDevices) return GGO_ERR_NO_DEVICE;
+  // Bind the device's primary context to this thread: the tensor-map encoder is a driver call and
+  // needs a current context, which a fresh thread (e.g. autograd's backward worker) lacks.
+  if (cudaError_t e = cudaSetDevice(dev)) return cuda_fail(e);
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_sm_count[dev] == 0) {
     int major = 0, sms = 0;
