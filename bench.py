@@ -344,6 +344,22 @@ def config_sweep(steps=20, warmup=3):
                      "tokens_per_expert_max": int(tpe.max())}
         del x, w
         torch.cuda.empty_cache()
+    # backward of the cfg2 grouped GEMM: dgrad (dx = dy W[e]) and wgrad (dW[e] = dy_e^T x_e)
+    from grouped_gemm_opt import _C
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(T_TOK, K, device="cuda", generator=g).to(torch.bfloat16)
+    dy = torch.randn(T_TOK, N, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    td = torch.full((E,), T_TOK // E, dtype=torch.int64, device="cuda")
+    for name, fn in (("cfg2_dgrad", lambda: _C.grouped_gemm_dgrad(dy, w, td, 4, True)),
+                     ("cfg2_wgrad", lambda: _C.grouped_gemm_wgrad(x, dy, td, True))):
+        for _ in range(warmup):
+            fn()
+        total, _ = _timed(fn, steps, 1)
+        ms = total / steps
+        res[name] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
+    del x, dy, w
+    torch.cuda.empty_cache()
     # DeepSeek-V3-shaped layer on one GPU (all 256 experts local): decode and prefill token counts
     for name, T in (("dsv3_layer_T256", 256), ("dsv3_layer_T32768", 32768)):
         H, F, ex, k = 7168, 2048, 256, 8
