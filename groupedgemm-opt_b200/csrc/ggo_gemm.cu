@@ -288,33 +288,45 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   // records a timeout in the workspace and returns; nothing faults or hangs.
   p.inject_stall = env_int("GGO_TEST_INJECT_STALL", 0) > 0 ? 1 : 0;
   p.wait_limit = p.inject_stall ? (1ll << 24) : GGO_WAIT_LIMIT_CYCLES;
+  p.split_mode = 0;
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.origin = scatter ? ex->origin : nullptr;
   for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;
   p.out = output;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
-  const int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
+  int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
+  if (bn == 512) {
+    // CTA-pair pass over 256-row tiles, then (GGO_SPLIT_TAILS, default on) a single-CTA pass over
+    // the segments' short tails (count mod 256 in 1..128), which would waste most of a pair tile.
+    const bool split = env_int("GGO_SPLIT_TAILS", 1) > 0;
+    GemmParams pp = p;
+    pp.group_m = raster_group_m(k, 256);
+    pp.split_mode = split ? 1 : 0;
+    int st;
+    if (bmn)
+      st = bf16 ? launch_pair<256, kEpiStore, true, true>(input, weights, b_rows, pp, dev, stream)
+                : launch_pair<256, kEpiStore, false, true>(input, weights, b_rows, pp, dev, stream);
+    else if (swiglu)
+      st = bf16 ? launch_pair_bn<kEpiSwiGLU, true>(env_int("GGO_PAIR_BN", kDefaultPairBN), input,
+                                                  weights, b_rows, pp, dev, stream)
+                : launch_pair_bn<kEpiSwiGLU, false>(env_int("GGO_PAIR_BN", kDefaultPairBN), input,
+                                                   weights, b_rows, pp, dev, stream);
+    else
+      st = bf16 ? launch_pair_bn<kEpiStore, true>(env_int("GGO_PAIR_BN", kDefaultPairBN), input,
+                                                 weights, b_rows, pp, dev, stream)
+                : launch_pair_bn<kEpiStore, false>(env_int("GGO_PAIR_BN", kDefaultPairBN), input,
+                                                  weights, b_rows, pp, dev, stream);
+    if (st || !split) return st;
+    p.split_mode = 2;
+    bn = 256;
+  }
   if (bmn) {  // dgrad form: MN-major weights, plain epilogue
-    if (bn == 512) {
-      p.group_m = raster_group_m(k, 256);
-      return bf16 ? launch_pair<256, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
-                  : launch_pair<256, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
-    }
     if (bn == 256)
       return bf16 ? launch<256, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
                   : launch<256, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
     return bf16 ? launch<128, kEpiStore, true, true>(input, weights, b_rows, p, dev, stream)
                 : launch<128, kEpiStore, false, true>(input, weights, b_rows, p, dev, stream);
-  }
-  if (bn == 512) {
-    p.group_m = raster_group_m(k, 256);
-    const int pbn = env_int("GGO_PAIR_BN", kDefaultPairBN);
-    if (swiglu)
-      return bf16 ? launch_pair_bn<kEpiSwiGLU, true>(pbn, input, weights, b_rows, p, dev, stream)
-                  : launch_pair_bn<kEpiSwiGLU, false>(pbn, input, weights, b_rows, p, dev, stream);
-    return bf16 ? launch_pair_bn<kEpiStore, true>(pbn, input, weights, b_rows, p, dev, stream)
-                : launch_pair_bn<kEpiStore, false>(pbn, input, weights, b_rows, p, dev, stream);
   }
   if (swiglu)
     return bf16 ? launch<256, kEpiSwiGLU, true>(input, weights, b_rows, p, dev, stream)

@@ -78,6 +78,7 @@ struct GemmParams {
   int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
   long long wait_limit;   // bounded-wait limit in SM cycles
   int inject_stall;       // test hook: CTA 0 never arms its first pipeline stage
+  int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
   GgoWorkspace* ws;
 };
 
@@ -143,6 +144,23 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
     }
     const bool bad = p.rows_is_bound ? carry > p.rows : carry != p.rows;
     if (lane == 0 && bad && blockIdx.x == 0) atomicCAS(err, 0, kDevCountMismatch);
+  }
+  if (p.split_mode) {
+    // Split launch: a segment's last `small` rows (its count mod 256, when 1..128) go to a
+    // 128-row single-CTA pass (mode 2); everything else to the 256-row pair pass (mode 1).
+    __syncthreads();
+    for (int s = threadIdx.x; s < nseg; s += kThreads) {
+      const int c = t_cnt[s];
+      const int r = c % 256;
+      const int small = (r > 0 && r <= 128) ? r : 0;
+      if (p.split_mode == 1) {
+        t_cnt[s] = c - small;
+      } else {
+        t_rowoff[s] += c - small;
+        t_cnt[s] = small;
+      }
+    }
+    __syncthreads();
   }
   // Processing order: identity, or heaviest segment first (ties by index) via a bitonic sort of
   // 64-bit keys held temporarily in the (still unused) operand tile buffers.

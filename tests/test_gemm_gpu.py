@@ -306,3 +306,14 @@ def test_autograd_matches_torch_reference(ggo):
             assert (wd.grad[e] == 0).all()
         else:
             assert_parity(wd.grad[e], wr.grad[e], f"grad weight {e}")
+
+
+@pytest.mark.parametrize("split", ["0", "1"])
+def test_split_tail_launch(ggo, split, monkeypatch):
+    """Pair pass + single-CTA pass over short segment tails (count mod 256 in 1..128)."""
+    monkeypatch.setenv("GGO_SPLIT_TAILS", split)
+    counts = [256 * 3 + 5, 128, 129, 0, 256, 383, 384, 1, 600]
+    x, w, tpe = gemm_inputs(counts, 256, 512, seed=9)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), 3)
+    assert_parity(out, ref, f"split={split}")
