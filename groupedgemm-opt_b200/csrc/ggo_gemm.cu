@@ -289,6 +289,8 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.inject_stall = env_int("GGO_TEST_INJECT_STALL", 0) > 0 ? 1 : 0;
   p.wait_limit = p.inject_stall ? (1ll << 24) : GGO_WAIT_LIMIT_CYCLES;
   p.split_mode = 0;
+  p.split_tail_ntiles = 1;
+  p.split_min_tiles = 0;
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.origin = scatter ? ex->origin : nullptr;
   for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;
@@ -300,6 +302,8 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
     // CTA-pair pass over 256-row tiles, then (GGO_SPLIT_TAILS, default on) a single-CTA pass over
     // the segments' short tails (count mod 256 in 1..128), which would waste most of a pair tile.
     const bool split = env_int("GGO_SPLIT_TAILS", 1) > 0;
+    p.split_tail_ntiles = static_cast<int>((n + (swiglu ? 127 : 255)) / (swiglu ? 128 : 256));
+    p.split_min_tiles = env_int("GGO_SPLIT_MIN_TILES", 2 * g_sm_count[dev]);
     GemmParams pp = p;
     pp.group_m = raster_group_m(k, 256);
     pp.split_mode = split ? 1 : 0;

@@ -79,6 +79,8 @@ struct GemmParams {
   long long wait_limit;   // bounded-wait limit in SM cycles
   int inject_stall;       // test hook: CTA 0 never arms its first pipeline stage
   int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
+  int split_tail_ntiles;  // column tiles of the tail pass (its output width / its tile width)
+  int split_min_tiles;    // split only when the tail pass gets at least this many tiles
   GgoWorkspace* ws;
 };
 
@@ -106,6 +108,20 @@ struct SmemLayout {
       1024 /*align slack*/ + kTileBytes + kStagingBytes + kTableBytes + kMiscBytes;
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
+
+// Sum of one int per thread over the CTA (all kThreads threads must call it).
+__device__ __forceinline__ int block_sum(int v) {
+  __shared__ int partial[kThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int t = 0;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) t += partial[i];
+  __syncthreads();
+  return t;
+}
 
 // Builds, in shared memory, the segment table every CTA needs to map a flat tile index to work:
 // clamped counts, exclusive row offsets (segment order), processing order (identity or heaviest
@@ -147,12 +163,22 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
   }
   if (p.split_mode) {
     // Split launch: a segment's last `small` rows (its count mod 256, when 1..128) go to a
-    // 128-row single-CTA pass (mode 2); everything else to the 256-row pair pass (mode 1).
+    // 128-row single-CTA pass (mode 2); everything else to the 256-row pair pass (mode 1). Both
+    // kernels take the same decision from the same counts: split only when the short tails make
+    // at least p.split_min_tiles single-CTA tiles (a tail pass of whole waves), else the pair
+    // pass keeps every row and the tail pass has nothing to do.
     __syncthreads();
+    int mine = 0;
+    for (int s = threadIdx.x; s < nseg; s += kThreads) {
+      const int r = t_cnt[s] % 256;
+      mine += (r > 0 && r <= 128) ? 1 : 0;
+    }
+    const int tails = block_sum(mine);
+    const bool split = static_cast<long long>(tails) * p.split_tail_ntiles >= p.split_min_tiles;
     for (int s = threadIdx.x; s < nseg; s += kThreads) {
       const int c = t_cnt[s];
       const int r = c % 256;
-      const int small = (r > 0 && r <= 128) ? r : 0;
+      const int small = (split && r > 0 && r <= 128) ? r : 0;
       if (p.split_mode == 1) {
         t_cnt[s] = c - small;
       } else {

@@ -312,6 +312,7 @@ def test_autograd_matches_torch_reference(ggo):
 def test_split_tail_launch(ggo, split, monkeypatch):
     """Pair pass + single-CTA pass over short segment tails (count mod 256 in 1..128)."""
     monkeypatch.setenv("GGO_SPLIT_TAILS", split)
+    monkeypatch.setenv("GGO_SPLIT_MIN_TILES", "1")  # split even this small problem
     counts = [256 * 3 + 5, 128, 129, 0, 256, 383, 384, 1, 600]
     x, w, tpe = gemm_inputs(counts, 256, 512, seed=9)
     ref = oracle.sequential_gemm(x, w, tpe)
