@@ -109,9 +109,10 @@ struct SmemLayout {
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-// Sum of one int per thread over the CTA (all kThreads threads must call it).
-__device__ __forceinline__ int block_sum(int v) {
-  __shared__ int partial[kThreads / 32];
+// Sum of one int per thread over the CTA (all kThreads threads must call it). `partial` is
+// kThreads / 32 ints of shared memory free for the duration of the call (no static shared memory:
+// it would push the 1024-aligned dynamic region past the per-CTA limit).
+__device__ __forceinline__ int block_sum(int v, int* partial) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = v;
@@ -173,7 +174,7 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
       const int r = t_cnt[s] % 256;
       mine += (r > 0 && r <= 128) ? 1 : 0;
     }
-    const int tails = block_sum(mine);
+    const int tails = block_sum(mine, t_tileoff);  // t_tileoff is filled later
     const bool split = static_cast<long long>(tails) * p.split_tail_ntiles >= p.split_min_tiles;
     for (int s = threadIdx.x; s < nseg; s += kThreads) {
       const int c = t_cnt[s];
