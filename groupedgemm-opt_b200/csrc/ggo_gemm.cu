@@ -291,7 +291,6 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.split_mode = 0;
   p.split_tail_ntiles = 1;
   p.split_min_tiles = 0;
-  p.interleave = env_int("GGO_INTERLEAVE", 1) > 0 ? 1 : 0;
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.origin = scatter ? ex->origin : nullptr;
   for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;

@@ -81,7 +81,6 @@ struct GemmParams {
   int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
   int split_tail_ntiles;  // column tiles of the tail pass (its output width / its tile width)
   int split_min_tiles;    // split only when the tail pass gets at least this many tiles
-  int interleave;         // interleave light (one-m-tile) segments among heavy ones
   GgoWorkspace* ws;
 };
 
@@ -132,8 +131,7 @@ __device__ __forceinline__ int block_sum(int v, int* partial) {
 template <int TILE_M, int OUT_BN>
 __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t* tiles, int* t_cnt,
                                                     int* t_rowoff, int* t_order, int* t_tileoff,
-                                                    int* total_tiles_s, int* err,
-                                                    int* heavy_tiles_s) {
+                                                    int* total_tiles_s, int* err) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nseg = p.num_segments;
@@ -243,20 +241,6 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
     if (lane == 0) {
       t_tileoff[nseg] = carry;
       *total_tiles_s = carry;
-      *heavy_tiles_s = carry;
-    }
-    __syncwarp();
-    // Heaviest-first order puts the segments of several m-tiles ("heavy", compute-bound) before
-    // the one-tile segments ("light", weight-streaming); record where the light ones start.
-    if (p.sort_by_m) {
-      for (int base = 0; base < nseg; base += 32) {
-        const int i = base + lane;
-        if (i < nseg) {
-          const bool light = t_cnt[t_order[i]] <= TILE_M;
-          const bool prev_heavy = i == 0 || t_cnt[t_order[i - 1]] > TILE_M;
-          if (light && prev_heavy) *heavy_tiles_s = t_tileoff[i];
-        }
-      }
     }
   }
 }
@@ -264,18 +248,6 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
 // Maps flat tile index t (< total tiles) to its rows, output columns and weight rows.
 // Tiles of one segment are rastered in groups of p.group_m m-tiles: inside a group the m index
 // runs fastest, so concurrently running CTAs share the weight tile in L2.
-// Claim order -> tile position. With interleaving, light tiles (weight-streaming, HBM-bound) are
-// spread evenly among heavy ones (compute-bound) so both the tensor pipes and HBM stay busy;
-// a Bresenham-style split of [0, total) that is a bijection onto heavy [0, heavy) and light
-// [heavy, total) positions.
-__device__ __forceinline__ int interleave_pos(int t, int total, int heavy, int enabled) {
-  const long long tl = total - heavy;
-  if (!enabled || tl == 0 || heavy == 0) return t;
-  const long long l0 = static_cast<long long>(t) * tl / total;
-  const long long l1 = static_cast<long long>(t + 1) * tl / total;
-  return l1 > l0 ? heavy + static_cast<int>(l0) : t - static_cast<int>(l0);
-}
-
 // After an abort, waits (bounded by `limit` cycles per stage) for the bulk loads this producer
 // issued into stages the MMA never consumed, so no copy is still landing in shared memory when the
 // CTA exits. Stage s was last armed with phase parity bit s of `armed_par`.
@@ -470,7 +442,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
   int* total_tiles_s = reinterpret_cast<int*>(tmem_slot + 1);
-  int* heavy_tiles_s = reinterpret_cast<int*>(tmem_slot + 2);
   WaitGuard* guard = reinterpret_cast<WaitGuard*>(tmem_slot + 4);  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
@@ -502,14 +473,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
 
-  build_segment_table<kBM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff, total_tiles_s,
-                                   err, heavy_tiles_s);
+  build_segment_table<kBM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff, total_tiles_s, err);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
-  const int heavy_tiles = *heavy_tiles_s;
   const int num_kb = (p.k + kBK - 1) / kBK;
 
   if (warp == 0) {
@@ -523,9 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         TileInfo info;
         info.rows = 0;
         if (t < total_tiles)
-          info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(
-              interleave_pos(t, total_tiles, heavy_tiles, p.interleave), p, t_cnt, t_rowoff,
-              t_order, t_tileoff);
+          info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);

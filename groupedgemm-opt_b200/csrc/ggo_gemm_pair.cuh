@@ -70,7 +70,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   TileInfo* ring = reinterpret_cast<TileInfo*>(sche_bar + kSchedDepth);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + kSchedDepth);
   int* total_tiles_s = reinterpret_cast<int*>(tmem_slot + 1);
-  int* heavy_tiles_s = reinterpret_cast<int*>(tmem_slot + 2);
   WaitGuard* guard = reinterpret_cast<WaitGuard*>(tmem_slot + 4);  // 16-byte aligned
 
   const int warp = threadIdx.x >> 5;
@@ -103,14 +102,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tmem_relinquish_pair();
   }
   build_segment_table<kTileM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff,
-                                      total_tiles_s, err, heavy_tiles_s);
+                                      total_tiles_s, err);
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
-  const int heavy_tiles = *heavy_tiles_s;
   const int num_kb = (p.k + kBK - 1) / kBK;
 
   if (warp == 0) {
@@ -125,9 +123,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int t = atomicAdd(&p.ws->tile_counter, 1);
           info.rows = 0;
           if (t < total_tiles)
-            info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(
-                interleave_pos(t, total_tiles, heavy_tiles, p.interleave), p, t_cnt, t_rowoff,
-                t_order, t_tileoff);
+            info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(t, p, t_cnt, t_rowoff, t_order,
+                                                               t_tileoff);
           if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer))
             break;
           ring[q] = info;
