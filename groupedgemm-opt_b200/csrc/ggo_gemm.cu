@@ -48,19 +48,30 @@ int get_encode(EncodeTiledFn* fn) {
 
 // 2D K-major operand map: dims {K, rows}, box {64, box_rows}, 128-B swizzle, zero fill out of
 // bounds.
-int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
-             int box_cols = kBK) {
+int make_map_dt(CUtensorMap* m, const void* base, int64_t rows, int64_t k,
+                CUtensorMapDataType dt, int elem_bytes, int box_rows, int box_cols) {
   EncodeTiledFn enc;
   if (int st = get_encode(&enc)) return st;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * elem_bytes};
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                   const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? GGO_OK : cuda_fail(100000 + static_cast<int>(r));
+}
+
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
+             int box_cols = kBK) {
+  return make_map_dt(m, base, rows, k,
+                     bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                     box_rows, box_cols);
+}
+
+// Operand map for 1-byte e4m3 data: rows of K bytes, boxes of 128 elements (128 B) x box_rows.
+int make_map_fp8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int box_rows) {
+  return make_map_dt(m, base, rows, k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, box_rows, 128);
 }
 
 // Output map for the TMA-store epilogue: [rows, n_out] row-major, boxes of 32 rows x 64 columns
@@ -112,15 +123,20 @@ int make_b_map(CUtensorMap* m, const void* b, int64_t b_rows, const GemmParams& 
   return make_map(m, b, b_rows, q.k, bf16, box_rows);
 }
 
-template <int BN, int EPI, bool BF16, bool BMN = false>
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
            cudaStream_t stream) {
   CUtensorMap ma, mb, mc;
   GemmParams q = p;
-  if (int st = make_map(&ma, a, q.rows, q.k, BF16, kBM)) return st;
-  if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, 128)) return st;
+  if (FP8) {
+    if (int st = make_map_fp8(&ma, a, q.rows, q.k, kBM)) return st;
+    if (int st = make_map_fp8(&mb, b, b_rows, q.k, 128)) return st;
+  } else {
+    if (int st = make_map(&ma, a, q.rows, q.k, BF16, kBM)) return st;
+    if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, 128)) return st;
+  }
   if (int st = make_out_map(&mc, &q, BF16)) return st;
-  auto kern = grouped_gemm_kernel<BN, EPI, BF16, BMN>;
+  auto kern = grouped_gemm_kernel<BN, EPI, BF16, BMN, FP8>;
   constexpr int smem = SmemLayout<BN>::kTotal;
   int sms = 0;
   if (int st = kernel_setup(kern, smem, dev, false, &sms)) return st;
@@ -133,15 +149,20 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   return check_launch();
 }
 
-template <int BN, int EPI, bool BF16, bool BMN = false>
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
                 cudaStream_t stream) {
   CUtensorMap ma, mb, mc;
   GemmParams q = p;
-  if (int st = make_map(&ma, a, q.rows, q.k, BF16, 128)) return st;
-  if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, BN / 2)) return st;
+  if (FP8) {
+    if (int st = make_map_fp8(&ma, a, q.rows, q.k, 128)) return st;
+    if (int st = make_map_fp8(&mb, b, b_rows, q.k, BN / 2)) return st;
+  } else {
+    if (int st = make_map(&ma, a, q.rows, q.k, BF16, 128)) return st;
+    if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, BN / 2)) return st;
+  }
   if (int st = make_out_map(&mc, &q, BF16)) return st;
-  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16, BMN>;
+  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16, BMN, FP8>;
   constexpr int smem = PairLayout<BN>::kTotal;
   int clusters = 0;
   if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
@@ -237,10 +258,14 @@ int choose_bn(int tile_config, int64_t rows, int64_t n, int num_segments, int sm
 
 // Expert-parallel extensions of one call (see ggo_ep_grouped_gemm).
 struct GemmExtras {
-  int rows_is_bound;
-  const int32_t* origin;
-  void* const* peer_out;
-  int world;
+  int rows_is_bound = 0;
+  const int32_t* origin = nullptr;
+  void* const* peer_out = nullptr;
+  int world = 1;
+  // FP8 path: e4m3 operands, out = acc * row_scale[row] * col_scale[expert * n + col] in bf16
+  int fp8 = 0;
+  const float* row_scale = nullptr;
+  const float* col_scale = nullptr;
 };
 
 int gemm_common(const void* input, const void* weights, void* output, const int64_t* counts,
@@ -261,6 +286,12 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
     return GGO_ERR_INVALID_ARG;
   if (tile_config < 0 || tile_config > GGO_TILE_CUBLAS_SEQ) return GGO_ERR_INVALID_ARG;
   if (num_segments > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
+  const bool fp8 = ex && ex->fp8;
+  if (fp8) {
+    if (!ex->row_scale || !ex->col_scale || swiglu || bmn || scatter) return GGO_ERR_INVALID_ARG;
+    dtype = GGO_DTYPE_BF16;  // e4m3 in, bf16 out
+    if (k % 16) return GGO_ERR_ALIGNMENT;  // rows of K bytes must be 16-byte multiples
+  }
   if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
   if ((k % 8) || (n % 8)) return GGO_ERR_ALIGNMENT;
   if (!aligned16(input) || !aligned16(weights) || (output && !aligned16(output)) ||
@@ -292,12 +323,30 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.split_tail_ntiles = 1;
   p.split_min_tiles = 0;
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
+  p.row_scale = fp8 ? ex->row_scale : nullptr;
+  p.col_scale = fp8 ? ex->col_scale : nullptr;
   p.origin = scatter ? ex->origin : nullptr;
   for (int r = 0; r < 8; ++r) p.peer_out[r] = (scatter && r < ex->world) ? ex->peer_out[r] : nullptr;
   p.out = output;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
+  if (fp8) {  // CTA-pair pass (+ short-tail pass) or single-CTA 128x256, scaled epilogue
+    if (bn == 512) {
+      const bool split = env_int("GGO_SPLIT_TAILS", 1) > 0;
+      p.split_tail_ntiles = static_cast<int>((n + 255) / 256);
+      p.split_min_tiles = env_int("GGO_SPLIT_MIN_TILES", 2 * g_sm_count[dev]);
+      GemmParams pp = p;
+      pp.group_m = raster_group_m(k / 2, 256);  // k bytes: half the bf16 panel size
+      pp.split_mode = split ? 1 : 0;
+      if (int st = launch_pair<256, kEpiScaled, true, false, true>(input, weights, b_rows, pp,
+                                                                   dev, stream))
+        return st;
+      if (!split) return GGO_OK;
+      p.split_mode = 2;
+    }
+    return launch<256, kEpiScaled, true, false, true>(input, weights, b_rows, p, dev, stream);
+  }
   if (bn == 512) {
     // CTA-pair pass over 256-row tiles, then (GGO_SPLIT_TAILS, default on) a single-CTA pass over
     // the segments' short tails (count mod 256 in 1..128), which would waste most of a pair tile.
@@ -504,6 +553,20 @@ int ggo_grouped_gemm_wgrad(const void* x_dev, const void* dy_dev, void* dw_dev,
                            void* workspace_dev, cudaStream_t stream) {
   return ggo::wgrad_common(x_dev, dy_dev, dw_dev, tokens_per_expert_dev, num_experts,
                            total_tokens, N, K, dtype, sort_by_m, workspace_dev, stream);
+}
+
+int ggo_grouped_gemm_fp8(const void* input_dev, const float* input_scale_dev,
+                         const void* weights_dev, const float* weight_scale_dev, void* output_dev,
+                         const int64_t* tokens_per_expert_dev, int num_experts,
+                         int64_t total_tokens, int64_t N, int64_t K, int tile_config,
+                         int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  ggo::GemmExtras ex;
+  ex.fp8 = 1;
+  ex.row_scale = input_scale_dev;
+  ex.col_scale = weight_scale_dev;
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_expert_dev, num_experts,
+                          num_experts, total_tokens, N, K, GGO_DTYPE_BF16, tile_config, sort_by_m,
+                          workspace_dev, stream, false, &ex);
 }
 
 int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,

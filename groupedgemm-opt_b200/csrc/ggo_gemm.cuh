@@ -38,7 +38,8 @@ constexpr int kMaxSegments = 1024;
 constexpr int kSchedDepth = 4;
 constexpr int kThreads = 256;
 
-enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1 };
+// kEpiScaled: out = acc * row_scale[row] * col_scale[expert * n_out + col] (the FP8 path).
+enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScaled = 2 };
 
 // Error codes written to GgoWorkspace::error (first error wins).
 enum DevError {
@@ -78,6 +79,8 @@ struct GemmParams {
   int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
   long long wait_limit;   // bounded-wait limit in SM cycles
   int inject_stall;       // test hook: CTA 0 never arms its first pipeline stage
+  const float* row_scale; // kEpiScaled: one scale per input row
+  const float* col_scale; // kEpiScaled: [num_experts, n_out] scales
   int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
   int split_tail_ntiles;  // column tiles of the tail pass (its output width / its tile width)
   int split_min_tiles;    // split only when the tail pass gets at least this many tiles
@@ -317,8 +320,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 // 32 output columns of this thread's accumulator row, packed as 16 bf16x2/half2 words: TMEM
 // columns [c, c+32) (plain), or silu(gate) * up from columns [c, c+32) and [BN/2 + c, ...).
 template <int BN, int EPI, bool BF16>
-__device__ __forceinline__ void load_out32(uint32_t t_row, int c, uint32_t (&o)[16]) {
-  if (EPI == kEpiStore) {
+__device__ __forceinline__ void load_out32(uint32_t t_row, int c, uint32_t (&o)[16], float rs = 1.f,
+                                           const float* cs = nullptr, int cs_valid = 0) {
+  if (EPI == kEpiScaled) {
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(t_row + c, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float s0 = 2 * i < cs_valid ? __ldg(cs + 2 * i) : 0.f;
+      const float s1 = 2 * i + 1 < cs_valid ? __ldg(cs + 2 * i + 1) : 0.f;
+      o[i] = pack2(__uint_as_float(v[2 * i]) * rs * s0, __uint_as_float(v[2 * i + 1]) * rs * s1,
+                   BF16);
+    }
+  } else if (EPI == kEpiStore) {
     uint32_t v[32];
     tmem_ld_32x32b_x32(t_row + c, v);
     tmem_ld_wait();
@@ -357,7 +372,8 @@ template <int BN, int EPI, bool BF16, typename OutT>
 __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_out, bool row_ok,
                                                 OutT* out_row, bool warp_tma,
                                                 const CUtensorMap* tmC, uint8_t* stage,
-                                                int x_row0) {
+                                                int x_row0, float rs = 1.f,
+                                                const float* cs_row = nullptr) {
   constexpr int OUTW = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
   const int lane = threadIdx.x & 31;
   const uint32_t st_row = smem_u32(stage) + lane * 128;
@@ -372,7 +388,8 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
       const int c = c64 + 32 * s;
       if (c >= OUTW) break;
       uint32_t o[16];
-      load_out32<BN, EPI, BF16>(t_row, c, o);
+      load_out32<BN, EPI, BF16>(t_row, c, o, rs, cs_row ? cs_row + n0 + c : nullptr,
+                                n_out - (n0 + c));
       if (warp_tma) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -412,7 +429,7 @@ __device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo&
   return reinterpret_cast<OutT*>(p.peer_out[src]) + static_cast<size_t>(p.origin[r]) * p.n_out;
 }
 
-template <int BN, int EPI, bool BF16, bool BMN = false>
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
@@ -479,7 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
-  const int num_kb = (p.k + kBK - 1) / kBK;
+  // K elements per pipeline stage: one 128-B swizzle row (64 bf16/fp16 or 128 e4m3)
+  constexpr int kStageK = FP8 ? 128 : kBK;
+  const int num_kb = (p.k + kStageK - 1) / kStageK;
 
   if (warp == 0) {
     // -------------------------------------------------------------- TMA producer
@@ -510,16 +529,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* a_dst = tiles + stage * L::kStageBytes;
             uint8_t* b_dst = a_dst + L::kABytes;
             mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, info.row0);
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kStageK, info.row0);
             if (BMN) {  // BN/64 boxes of [64 reduction rows][64 output columns]
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i)
                 tma_load_2d(b_dst + i * 8192, &tmB, &full_bar[stage], info.n0 + 64 * i,
                             info.brow0 + kb * kBK);
             } else {
-              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kBK, info.brow0);
+              tma_load_2d(b_dst, &tmB, &full_bar[stage], kb * kStageK, info.brow0);
               if (BN == 256)
-                tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kBK, info.brow1);
+                tma_load_2d(b_dst + 128 * 128, &tmB, &full_bar[stage], kb * kStageK, info.brow1);
             }
             armed |= 1u << stage;
             armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
@@ -534,7 +553,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kBM, BN, BF16, BMN);
+      // e4m3 operands are format 0 of kind::f8f6f4, the same bits as f16 in kind::f16
+      constexpr uint32_t idesc = idesc_f16(kBM, BN, FP8 ? false : BF16, BMN);
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
@@ -561,8 +581,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // B likewise, an MN-major B by 16 rows of 128 B (two 8-row atoms)
           constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-            mma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {  // four 32-byte K steps per 128-byte stage row
+            if (FP8)
+              mma_f8_ss(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+            else
+              mma_f16_ss(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+          }
           mma_commit(&empty_bar[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -590,8 +614,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       const bool warp_tma = kTmaStoreOk && p.use_tma_store && ew * 32 + 32 <= info.rows;
+      const float rs = (EPI == kEpiScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
+      const float* cs_row = EPI == kEpiScaled
+                                ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_out
+                                : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
-                                     staging + ew * 4096, info.row0 + ew * 32);
+                                     staging + ew * 4096, info.row0 + ew * 32, rs, cs_row);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);

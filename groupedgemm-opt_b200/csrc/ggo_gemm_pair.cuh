@@ -36,7 +36,7 @@ struct PairLayout {
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, int EPI, bool BF16, bool BMN = false>
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
@@ -109,7 +109,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
-  const int num_kb = (p.k + kBK - 1) / kBK;
+  constexpr int kStageK = FP8 ? 128 : kBK;  // K elements per stage (one 128-B swizzle row)
+  const int num_kb = (p.k + kStageK - 1) / kStageK;
 
   if (warp == 0) {
     // -------------------------------------------------------------- TMA producers (both CTAs)
@@ -162,7 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
             }
             const uint32_t fb = mapa_shared(&full_bar[stage], 0);
-            tma_load_2d_pair(a_dst, &tmA, fb, kb * kBK, a_row);
+            tma_load_2d_pair(a_dst, &tmA, fb, kb * kStageK, a_row);
             if (BMN) {  // this CTA's BN/2 output columns as 64-column boxes
 #pragma unroll
               for (int i = 0; i < BN / 128; ++i)
@@ -170,7 +171,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                  info.n0 + static_cast<int>(rank) * (BN / 2) + 64 * i,
                                  info.brow0 + kb * kBK);
             } else {
-              tma_load_2d_pair(b_dst, &tmB, fb, kb * kBK, b_row);
+              tma_load_2d_pair(b_dst, &tmB, fb, kb * kStageK, b_row);
             }
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -185,7 +186,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // -------------------------------------------------------------- MMA issuer (leader only)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(kTileM, BN, BF16, BMN);
+      constexpr uint32_t idesc = idesc_f16(kTileM, BN, FP8 ? false : BF16, BMN);
       static_assert(!BMN || (BN / 2) % 64 == 0, "MN-major B halves are whole 64-column boxes");
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       const uint32_t tiles_addr = smem_u32(tiles);
@@ -211,8 +212,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                      : sdesc_sw128_kmajor(a_addr + L::kABytes);
           constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-            mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {  // four 32-byte K steps per 128-byte stage row
+            if (FP8)
+              mma_f8_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+            else
+              mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+          }
           mma_commit_pair(&empty_bar[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -241,8 +246,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       const int wrow0 = static_cast<int>(rank) * 128 + ew * 32;
       const bool warp_tma = kTmaStoreOk && p.use_tma_store && wrow0 + 32 <= info.rows;
+      const float rs = (EPI == kEpiScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
+      const float* cs_row = EPI == kEpiScaled
+                                ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_out
+                                : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
-                                     staging + ew * 4096, info.row0 + wrow0);
+                                     staging + ew * 4096, info.row0 + wrow0, rs, cs_row);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));

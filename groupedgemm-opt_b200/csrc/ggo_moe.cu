@@ -11,6 +11,7 @@
 // function of the routing: expert-major, then token index.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "ggo.h"
 #include "ggo_internal.h"
@@ -295,6 +296,47 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Per-row e4m3 quantisation: scale[r] = max|x[r,:]| / 448 (1 for an all-zero row) and
+// q[r,c] = e4m3(x[r,c] / scale[r]) rounded to nearest, saturating. One warp per row.
+template <typename T16>
+__global__ void __launch_bounds__(256)
+    quantize_rows_fp8_kernel(const T16* __restrict__ x, int rows, int cols,
+                             uint8_t* __restrict__ q, float* __restrict__ scale) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const T16* xr = x + static_cast<size_t>(r) * cols;
+  const int vec = cols / 8;
+  float amax = 0.f;
+  for (int c = lane; c < vec; c += 32) {
+    float f[8];
+    unpack8<T16>(reinterpret_cast<const uint4*>(xr)[c], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = amax > 0.f ? amax / 448.f : 1.f;
+  if (lane == 0) scale[r] = s;
+  uint8_t* qr = q + static_cast<size_t>(r) * cols;
+  for (int c = lane; c < vec; c += 32) {
+    float f[8];
+    unpack8<T16>(reinterpret_cast<const uint4*>(xr)[c], f);
+    uint32_t w[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t lo =
+          __nv_cvt_float2_to_fp8x2(make_float2(f[4 * h] / s, f[4 * h + 1] / s), __NV_SATFINITE,
+                                   __NV_E4M3);
+      const __nv_fp8x2_storage_t hi =
+          __nv_cvt_float2_to_fp8x2(make_float2(f[4 * h + 2] / s, f[4 * h + 3] / s),
+                                   __NV_SATFINITE, __NV_E4M3);
+      w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    reinterpret_cast<uint2*>(qr)[c] = make_uint2(w[0], w[1]);
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int nblocks_for(int64_t T) { return static_cast<int>((T + kRouteTokens - 1) / kRouteTokens); }
@@ -405,6 +447,25 @@ int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int n
   return ggo::dispatch_common(x_dev, num_tokens, hidden, num_experts, top_k, topk_ids_dev,
                               scratch_dev, counts_all_dev, world_size, rank, recv_rows,
                               recv_origin, nullptr, slot_pos_dev, dtype, stream);
+}
+
+int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dtype, void* q_dev,
+                          float* scale_dev, cudaStream_t stream) {
+  if (!x_dev || !q_dev || !scale_dev || rows < 0 || cols <= 0) return GGO_ERR_INVALID_ARG;
+  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
+  if (cols % 16 || !ggo::aligned16(x_dev) || !ggo::aligned16(q_dev)) return GGO_ERR_ALIGNMENT;
+  if (rows > INT32_MAX || cols > INT32_MAX) return GGO_ERR_SHAPE;
+  if (rows == 0) return GGO_OK;
+  const int grid = static_cast<int>((rows + 7) / 8);
+  if (dtype == GGO_DTYPE_BF16)
+    ggo::quantize_rows_fp8_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x_dev), static_cast<int>(rows), static_cast<int>(cols),
+        static_cast<uint8_t*>(q_dev), scale_dev);
+  else
+    ggo::quantize_rows_fp8_kernel<__half><<<grid, 256, 0, stream>>>(
+        static_cast<const __half*>(x_dev), static_cast<int>(rows), static_cast<int>(cols),
+        static_cast<uint8_t*>(q_dev), scale_dev);
+  return ggo::check_launch();
 }
 
 int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,

@@ -150,6 +150,53 @@ torch::Tensor grouped_gemm_wgrad(const torch::Tensor& x, const torch::Tensor& dy
   return dw;
 }
 
+// Row-wise e4m3 quantisation: returns (q float8_e4m3fn [rows, cols], scale fp32 [rows]).
+std::tuple<torch::Tensor, torch::Tensor> quantize_fp8_rows(const torch::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() >= 2, "x must be contiguous CUDA");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t cols = x.size(-1), rows = x.numel() / cols;
+  auto q = torch::empty(x.sizes(), x.options().dtype(torch::kFloat8_e4m3fn));
+  auto sizes = x.sizes().vec();
+  sizes.pop_back();
+  auto s = torch::empty(sizes, x.options().dtype(torch::kFloat32));
+  check_status(ggo_quantize_fp8_rows(x.data_ptr(), rows, cols, dtype_code(x), q.data_ptr(),
+                                     s.data_ptr<float>(), stream),
+               "fp8 quantisation");
+  return {q, s};
+}
+
+// FP8 grouped GEMM: out bf16 [T, N] = (a_q @ w_q[e]^T) * a_scale[row] * w_scale[e, col].
+torch::Tensor grouped_gemm_fp8(const torch::Tensor& a_q, const torch::Tensor& a_scale,
+                               const torch::Tensor& w_q, const torch::Tensor& w_scale,
+                               const torch::Tensor& tokens_per_expert, int64_t tile_config,
+                               bool sort_by_m) {
+  TORCH_CHECK(a_q.is_cuda() && w_q.is_cuda() && a_q.dim() == 2 && w_q.dim() == 3,
+              "a_q [T, K] and w_q [E, N, K] CUDA tensors");
+  TORCH_CHECK(a_q.scalar_type() == torch::kFloat8_e4m3fn &&
+                  w_q.scalar_type() == torch::kFloat8_e4m3fn, "operands must be float8_e4m3fn");
+  TORCH_CHECK(a_q.size(1) == w_q.size(2), "K mismatch");
+  TORCH_CHECK(a_q.is_contiguous() && w_q.is_contiguous(), "operands must be contiguous");
+  TORCH_CHECK(a_scale.scalar_type() == torch::kFloat32 && a_scale.numel() == a_q.size(0) &&
+                  a_scale.is_contiguous(), "a_scale must be fp32 [T]");
+  TORCH_CHECK(w_scale.scalar_type() == torch::kFloat32 &&
+                  w_scale.numel() == w_q.size(0) * w_q.size(1) && w_scale.is_contiguous(),
+              "w_scale must be fp32 [E, N]");
+  c10::cuda::CUDAGuard guard(a_q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = a_q.size(0), K = a_q.size(1), E = w_q.size(0), N = w_q.size(1);
+  auto out = torch::empty({T, N}, a_q.options().dtype(torch::kBFloat16));
+  if (T == 0) return out;
+  auto c = counts_on_device(tokens_per_expert, a_q.device());
+  const int st = ggo_grouped_gemm_fp8(
+      a_q.data_ptr(), a_scale.data_ptr<float>(), w_q.data_ptr(), w_scale.data_ptr<float>(),
+      out.data_ptr(), c.data_ptr<int64_t>(), static_cast<int>(E), T, N, K,
+      static_cast<int>(tile_config), sort_by_m ? 1 : 0, workspace_for(a_q.device(), stream),
+      stream);
+  check_status(st, "fp8 grouped GEMM");
+  return out;
+}
+
 torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
                                   const torch::Tensor& counts, int64_t num_experts,
                                   bool sort_by_m) {
@@ -453,6 +500,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("tokens_per_expert"), py::arg("tile_config") = 4, py::arg("sort_by_m") = true);
   m.def("grouped_gemm_wgrad", &grouped_gemm_wgrad, py::arg("x"), py::arg("dy"),
         py::arg("tokens_per_expert"), py::arg("sort_by_m") = true);
+  m.def("quantize_fp8_rows", &quantize_fp8_rows, py::arg("x"));
+  m.def("grouped_gemm_fp8", &grouped_gemm_fp8, py::arg("input_q"), py::arg("input_scale"),
+        py::arg("weights_q"), py::arg("weight_scale"), py::arg("tokens_per_expert"),
+        py::arg("tile_config") = 4, py::arg("sort_by_m") = true);
   m.def("grouped_gemm_swiglu", &grouped_gemm_swiglu, py::arg("x"), py::arg("w_gate_up"),
         py::arg("tokens_per_segment"), py::arg("num_experts"), py::arg("sort_by_m") = true);
   m.def("moe_route", &moe_route, py::arg("router_logits"), py::arg("top_k"));

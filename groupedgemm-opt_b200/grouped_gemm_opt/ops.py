@@ -135,3 +135,33 @@ def grouped_gemm_opt_host(
                           pin_memory=True)
     return _C.grouped_gemm_host(input.contiguous(), weights.contiguous(),
                                 tokens_per_expert, out, int(tile_config), sort_by_m, chunks)
+
+
+def quantize_fp8(x: torch.Tensor):
+    """Row-wise e4m3 quantisation on the GPU: returns (q float8_e4m3fn, scale fp32) with
+    x ~= q * scale[..., None]; scale = rowwise max|x| / 448. Weights [E, N, K] quantise per
+    output channel (scale [E, N])."""
+    return _C.quantize_fp8_rows(x.contiguous())
+
+
+def grouped_gemm_opt_fp8(
+    input_q: torch.Tensor,
+    input_scale: torch.Tensor,
+    weights_q: torch.Tensor,
+    weight_scale: torch.Tensor,
+    tokens_per_expert: torch.Tensor,
+    tile_config: TileConfig = TileConfig.AUTO,
+    sort_by_m: bool = True,
+) -> torch.Tensor:
+    """FP8 grouped GEMM: ``out[i] = (q_in[i] @ q_w[e(i)].T) * input_scale[i] * weight_scale[e(i)]``
+    with e4m3 operands (tcgen05 kind::f8f6f4, fp32 accumulation) and a bf16 result. Use
+    :func:`quantize_fp8` to produce the operands and scales."""
+    assert input_q.is_cuda and weights_q.is_cuda
+    tokens_per_expert = tokens_per_expert.to(torch.int64).contiguous()
+    if not tokens_per_expert.is_cuda:
+        total = int(tokens_per_expert.sum().item())
+        assert total == input_q.size(0), (
+            f"sum(tokens_per_expert)={total} != total_tokens={input_q.size(0)}")
+    return _C.grouped_gemm_fp8(input_q.contiguous(), input_scale.contiguous().float(),
+                               weights_q.contiguous(), weight_scale.contiguous().float(),
+                               tokens_per_expert, int(tile_config), sort_by_m)

@@ -123,6 +123,24 @@ int ggo_grouped_gemm_wgrad(const void* x_dev, const void* dy_dev, void* dw_dev,
                            int64_t total_tokens, int64_t N, int64_t K, int dtype, int sort_by_m,
                            void* workspace_dev, cudaStream_t stream);
 
+/* FP8 grouped GEMM (no reference counterpart; the reference is bf16/fp16 only):
+ *   out[r, n] = (sum_k a[r,k] * b[e(r),n,k]) * input_scale[r] * weight_scale[e(r), n]   (bf16)
+ * input_dev [T, K] and weights_dev [E, N, K] are e4m3 bytes (tcgen05 kind::f8f6f4, fp32
+ * accumulation); input_scale_dev [T] and weight_scale_dev [E, N] fp32 (see
+ * ggo_quantize_fp8_rows). K a multiple of 16, N of 8. Same segment rules as ggo_grouped_gemm. */
+int ggo_grouped_gemm_fp8(const void* input_dev, const float* input_scale_dev,
+                         const void* weights_dev, const float* weight_scale_dev, void* output_dev,
+                         const int64_t* tokens_per_expert_dev, int num_experts,
+                         int64_t total_tokens, int64_t N, int64_t K, int tile_config,
+                         int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
+/* Row-wise e4m3 quantisation of a bf16/fp16 matrix [rows, cols]: scale_dev[r] =
+ * max|x[r,:]| / 448 (1 for an all-zero row), q_dev[r,c] = e4m3(x[r,c] / scale[r]) rounded to
+ * nearest with saturation. Weights [E, N, K] quantise per output channel as rows = E*N.
+ * cols a multiple of 16. */
+int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dtype, void* q_dev,
+                          float* scale_dev, cudaStream_t stream);
+
 /* Fused-MoE stage 2: gate/up grouped GEMM with the SwiGLU epilogue.
  *   h[r, f] = silu(x[r,:] . Wgu[e, f, :]) * (x[r,:] . Wgu[e, F + f, :])
  * w_gate_up_dev [num_experts, 2F, K]: rows 0..F-1 gate, rows F..2F-1 up.
