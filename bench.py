@@ -358,7 +358,17 @@ def config_sweep(steps=20, warmup=3):
         total, _ = _timed(fn, steps, 1)
         ms = total / steps
         res[name] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
-    del x, dy, w
+    # FP8 (e4m3, per-row / per-channel scales) forward of the same cfg2 problem
+    from grouped_gemm_opt import grouped_gemm_opt_fp8, quantize_fp8
+    xq, xs = quantize_fp8(x)
+    wq, ws = quantize_fp8(w)
+    fn = lambda: grouped_gemm_opt_fp8(xq, xs, wq, ws, td)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    total, _ = _timed(fn, steps, 1)
+    ms = total / steps
+    res["cfg2_fp8"] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
+    del x, dy, w, xq, wq
     torch.cuda.empty_cache()
     # DeepSeek-V3-shaped layer on one GPU (all 256 experts local): decode and prefill token counts
     for name, T in (("dsv3_layer_T256", 256), ("dsv3_layer_T32768", 32768)):
