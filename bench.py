@@ -260,6 +260,7 @@ def moe_layer_bench(world, rank, steps, warmup):
 
 def profile_run(args):
     """`--profile gemm`: cfg2 grouped GEMM launches only (1 kernel per step).
+    `--profile fp8|dgrad|wgrad`: the FP8 forward / backward kernels on the cfg2 shapes.
     `--profile moe`: the single-GPU Mixtral layer (route, scan, permute, gate/up, down, combine).
     Used under ncu; prints nothing but a done line."""
     import torch
@@ -271,6 +272,20 @@ def profile_run(args):
         w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
         tpe = torch.full((E,), T_TOK // E, dtype=torch.int64, device="cuda")
         fn = lambda: ggo.grouped_gemm_opt(x, w, tpe)  # noqa: E731
+    elif args.profile in ("fp8", "dgrad", "wgrad"):
+        from grouped_gemm_opt import _C, grouped_gemm_opt_fp8, quantize_fp8
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(T_TOK, K, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        tpe = torch.full((E,), T_TOK // E, dtype=torch.int64, device="cuda")
+        if args.profile == "fp8":
+            xq, xs = quantize_fp8(x)
+            wq, ws = quantize_fp8(w)
+            fn = lambda: grouped_gemm_opt_fp8(xq, xs, wq, ws, tpe)  # noqa: E731
+        else:
+            dy = torch.randn(T_TOK, N, device="cuda", generator=g).to(torch.bfloat16)
+            fn = (lambda: _C.grouped_gemm_dgrad(dy, w, tpe, 4, True)) if args.profile == "dgrad" \
+                else (lambda: _C.grouped_gemm_wgrad(x, dy, tpe, True))
     else:
         T, H, F, Ex, k = 16384, 4096, 14336, 8, 2
         g = torch.Generator(device="cuda").manual_seed(1)
@@ -310,7 +325,7 @@ def _dirichlet_counts(total, experts, alpha=0.5, seed=0):
     return torch.from_numpy(rng.multinomial(total, rng.dirichlet(np.full(experts, alpha))))
 
 
-def config_sweep(steps=20, warmup=3):
+def config_sweep(steps=60, warmup=5):
     """The other BASELINE configs at N=1 (secondary numbers; the headline is cfg2 uniform):
     TFLOP/s of the grouped GEMM and, for the weight-bound ones, HBM GB/s of algorithmic bytes
     (activations + weights of non-empty experts + output) over the kernel time."""
@@ -402,7 +417,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the secondary-config sweep")
-    ap.add_argument("--profile", choices=["gemm", "moe"], default=None,
+    ap.add_argument("--profile", choices=["gemm", "moe", "fp8", "dgrad", "wgrad"], default=None,
                     help="minimal run for ncu captures: warm-up + steps of one path, no JSON")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
