@@ -406,7 +406,7 @@ int launch_wgrad(const void* x, const void* dy, void* dw, const WgradParams& p, 
   const int64_t tiles = static_cast<int64_t>(p.num_experts) * ((p.n + 127) / 128) *
                         ((p.k + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  kern<<<grid, kWgradThreads, smem, stream>>>(mdy, mx, mw, p);
+  kern<<<grid, kThreads, smem, stream>>>(mdy, mx, mw, p);
   return check_launch();
 }
 

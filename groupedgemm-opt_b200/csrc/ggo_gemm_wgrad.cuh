@@ -30,16 +30,14 @@ struct WgradParams {
   long long wait_limit;
 };
 
-constexpr int kWgradThreads = 384;  // warps 4..11: epilogue, two warps per TMEM lane quarter
-
 template <int BN>
 struct WgradLayout {
   static constexpr int kABytes = 128 * kBK * 2;  // two 64x64 boxes: 128 dW rows x 64 tokens
   static constexpr int kBBytes = BN * kBK * 2;   // BN/64 boxes: BN dW columns x 64 tokens
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 3 : 5;
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
   static constexpr int kTileBytes = kStages * kStageBytes;
-  static constexpr int kStagingBytes = 8 * 4096;  // 4 KB per epilogue warp
+  static constexpr int kStagingBytes = 4 * 4096;
   static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
   static constexpr int kTotal =
@@ -58,7 +56,7 @@ struct WgradTile {
 };
 
 template <int BN, bool BF16>
-__global__ void __launch_bounds__(kWgradThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_wgrad_kernel(const __grid_constant__ CUtensorMap tmDY,
                               const __grid_constant__ CUtensorMap tmX,
                               const __grid_constant__ CUtensorMap tmW, const WgradParams p) {
@@ -98,11 +96,11 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf_bar[i], 1);
-      mbar_init(&acce_bar[i], 8);
+      mbar_init(&acce_bar[i], 4);
     }
     for (int i = 0; i < kSchedDepth; ++i) {
       mbar_init(&schf_bar[i], 1);
-      mbar_init(&sche_bar[i], 1 + 8);
+      mbar_init(&sche_bar[i], 1 + 4);
     }
     guard->abort = 0;
     guard->limit = p.wait_limit;
@@ -115,7 +113,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
     tmem_relinquish();
   }
   // expert table: clamped counts, token offsets, heaviest-first order
-  for (int e = threadIdx.x; e < E; e += kWgradThreads) {
+  for (int e = threadIdx.x; e < E; e += kThreads) {
     long long c = p.counts[e];
     if (c < 0) {
       atomicCAS(err, 0, kDevNegativeCount);
@@ -142,14 +140,14 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
   }
   if (p.sort_by_m && E > 1) {  // rank of expert e in descending-count order (ties by index)
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += kWgradThreads) {
+    for (int e = threadIdx.x; e < E; e += kThreads) {
       int r = 0;
       const int ce = t_cnt[e];
       for (int j = 0; j < E; ++j) r += (t_cnt[j] > ce) || (t_cnt[j] == ce && j < e);
       t_order[r] = e;
     }
   } else {
-    for (int e = threadIdx.x; e < E; e += kWgradThreads) t_order[e] = e;
+    for (int e = threadIdx.x; e < E; e += kThreads) t_order[e] = e;
   }
   tc_fence_before();
   __syncthreads();
@@ -267,9 +265,8 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
       if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
   } else if (warp >= 4) {
-    // -------------------------------------------------------------- epilogue (8 warps)
-    const int ew = (warp - 4) % 4;    // TMEM lane quarter
-    const int half = (warp - 4) / 4;  // column half of the tile this warp stores
+    // -------------------------------------------------------------- epilogue
+    const int ew = warp - 4;
     int q = 0, qphase = 0, acc = 0, aphase = 0;
     while (true) {
       if (!mbar_wait(&schf_bar[q], qphase, guard, err, kDevTimeoutEpilogue)) break;
@@ -285,15 +282,12 @@ __global__ void __launch_bounds__(kWgradThreads, 1)
       const int grow = info.expert * p.n + info.m0;  // row of dW viewed as [E*N, K]
       OutT* out_row = reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(grow + r_local) * p.k;
       const bool warp_tma = ew * 32 + 32 <= info.rows;
-      const int c0 = half * (BN / 2);
       if (info.ntok > 0) {
-        const uint32_t t_row =
-            tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN + c0;
-        store_tile_rows<BN / 2, kEpiStore, BF16>(t_row, info.n0 + c0, p.k, row_ok, out_row,
-                                                 warp_tma, &tmW, staging + (warp - 4) * 4096,
-                                                 grow + ew * 32);
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
+        store_tile_rows<BN, kEpiStore, BF16>(t_row, info.n0, p.k, row_ok, out_row, warp_tma,
+                                             &tmW, staging + ew * 4096, grow + ew * 32);
       } else if (row_ok) {  // expert without tokens: zero gradient
-        for (int c = c0; c < c0 + BN / 2; c += 8)
+        for (int c = 0; c < BN; c += 8)
           if (info.n0 + c < p.k)
             *reinterpret_cast<uint4*>(out_row + info.n0 + c) = make_uint4(0u, 0u, 0u, 0u);
       }
