@@ -276,9 +276,8 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   if (!input || !weights || (!output && !scatter) || !counts || !workspace)
     return GGO_ERR_INVALID_ARG;
   if (scatter) {
-    if (ex->world < 1 || ex->world > 8 || num_segments % num_experts ||
-        num_segments / num_experts > ex->world)
-      return GGO_ERR_INVALID_ARG;
+    if (ex->world < 1 || ex->world > 8) return GGO_ERR_INVALID_ARG;
+    if (rows > 0x0fffffff) return GGO_ERR_SHAPE;  // origin words hold 28-bit row numbers
     for (int r = 0; r < ex->world; ++r)
       if (!ex->peer_out[r] || !aligned16(ex->peer_out[r])) return GGO_ERR_ALIGNMENT;
   }

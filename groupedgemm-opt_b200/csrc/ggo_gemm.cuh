@@ -73,7 +73,7 @@ struct GemmParams {
   void* out;              // [rows, n_out], bf16 or fp16
   int rows_is_bound;      // 1: `rows` is a capacity; counts may sum to less (no mismatch error)
   // Scatter epilogue (expert parallelism): when `origin` is set, output row r goes to
-  // peer_out[segment / num_experts] + origin[r] * n_out instead of out + r * n_out.
+  // peer_out[origin[r] >> 28] + (origin[r] & 0x0fffffff) * n_out instead of out + r * n_out.
   const int32_t* origin;
   void* peer_out[8];
   int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
@@ -425,8 +425,9 @@ __device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo&
   const int r = info.row0 + r_local;
   if (p.origin == nullptr || !row_ok)
     return reinterpret_cast<OutT*>(p.out) + static_cast<size_t>(r) * p.n_out;
-  const int src = info.seg / p.num_experts;
-  return reinterpret_cast<OutT*>(p.peer_out[src]) + static_cast<size_t>(p.origin[r]) * p.n_out;
+  const int o = p.origin[r];  // (source rank << 28) | row on the source rank
+  return reinterpret_cast<OutT*>(p.peer_out[(o >> 28) & 7]) +
+         static_cast<size_t>(o & 0x0fffffff) * p.n_out;
 }
 
 template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>

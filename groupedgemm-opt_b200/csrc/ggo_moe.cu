@@ -157,10 +157,10 @@ __global__ void __launch_bounds__(1024)
 
 // Where dispatched rows go. world == 1: recv[0] is the local expert-sorted buffer and a row's
 // destination is its sorted position. world > 1 (expert parallelism): rank r owns experts
-// [r*el, (r+1)*el); recv[r] is rank r's receive buffer (a peer mapping for r != rank) laid out as
-// [source rank][local expert] segments whose sizes come from counts_all [world][E]
-// (every rank's tokens_per_expert), and origin[r][dst] receives the row's sorted position on
-// the source rank (where its result must come back).
+// [r*el, (r+1)*el); recv[r] is rank r's receive buffer (a peer mapping for r != rank) laid out
+// expert-major, [local expert][source rank], with sizes from counts_all [world][E] (every rank's
+// tokens_per_expert), so each local expert is one contiguous segment; origin[r][dst] receives
+// (source rank << 28) | the row's sorted position on the source (where its result goes back).
 template <typename T16>
 struct DispatchTargets {
   int world;
@@ -194,13 +194,14 @@ __global__ void __launch_bounds__(kRouteThreads)
     if (tg.world == 1) {
       dbase[e] = expert_start[e];
     } else {
-      // rows from lower source ranks for the owner's experts, then this rank's rows for the
-      // owner's lower local experts
+      // owner's receive buffer is expert-major: all rows of its lower local experts (from every
+      // source), then this expert's rows from lower source ranks
       const int r = e / tg.el, le = e % tg.el;
       long long b = 0;
-      for (int s = 0; s < tg.rank; ++s)
-        for (int j = 0; j < tg.el; ++j) b += tg.counts_all[static_cast<size_t>(s) * E + r * tg.el + j];
-      for (int j = 0; j < le; ++j) b += tg.counts_all[static_cast<size_t>(tg.rank) * E + r * tg.el + j];
+      for (int j = 0; j < le; ++j)
+        for (int s = 0; s < tg.world; ++s)
+          b += tg.counts_all[static_cast<size_t>(s) * E + r * tg.el + j];
+      for (int s = 0; s < tg.rank; ++s) b += tg.counts_all[static_cast<size_t>(s) * E + e];
       dbase[e] = static_cast<int>(b);
     }
   }
@@ -224,7 +225,8 @@ __global__ void __launch_bounds__(kRouteThreads)
         drow[i] = d;
         slot_pos[static_cast<size_t>(t0) * K + i] = ps;
         if (sorted_token) sorted_token[ps] = t0 + i / K;
-        if (tg.world > 1) tg.origin[id / tg.el][d] = ps;
+        // origin word: source rank in bits 28..30, sorted position on the source below
+        if (tg.world > 1) tg.origin[id / tg.el][d] = (tg.rank << 28) | ps;
       }
       __syncwarp();
     }

@@ -19,7 +19,8 @@ for rank r are one contiguous run (experts are sorted globally). Per layer:
   2. one device->host read of the split sizes (the only host sync of the layer);
   3. all_to_all_single of the rows;
   4. the received rows are [source rank][local expert] segments -- fed directly to the grouped
-     GEMMs as segments (segment s uses local expert s % (E/P)), no re-sort;
+     GEMMs as segments (segment s uses local expert s % (E/P)), no re-sort (NCCL path; the fused
+     peer-memory path lays the receive buffer out expert-major, one segment per local expert);
   5. reverse all_to_all_single of the down-projection rows, back into the sender's sorted order;
   6. local combine.
 """
@@ -147,7 +148,8 @@ def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuf
     slot_pos = C.ep_dispatch(hidden, ids, scratch, counts_all, rank, bufs.ptrs["recv"],
                              bufs.ptrs["origin"])
     bufs.fence()
-    seg_counts = counts_all[:, rank * el:(rank + 1) * el].contiguous().view(-1)
+    # receive buffer is expert-major: one segment per local expert, rows from every source
+    seg_counts = counts_all[:, rank * el:(rank + 1) * el].sum(0)
     h = C.ep_grouped_gemm(bufs.recv, w_gate_up, seg_counts, el, True, None, [], sort_by_m)
     C.ep_grouped_gemm(h, w_down, seg_counts, el, False, bufs.origin, bufs.ptrs["back"],
                       sort_by_m)

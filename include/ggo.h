@@ -202,9 +202,10 @@ int ggo_ipc_free(void* ptr);
  * receive buffer of the rank owning its expert (rank r owns experts [r*E/P, (r+1)*E/P)).
  * counts_all_dev [P, E] int64: every rank's tokens_per_expert (e.g. an all_gather of them).
  * recv_rows[r] / recv_origin[r]: rank r's receive rows [capacity, H] and origin [capacity] int32,
- * as mapped in this process (own buffers for r == rank). Received rows are laid out as
- * [source rank][local expert] segments; recv_origin holds each row's sorted position on its
- * source rank. slot_pos_dev as in ggo_moe_permute. */
+ * as mapped in this process (own buffers for r == rank). Received rows are laid out
+ * expert-major, [local expert][source rank], so each local expert is one contiguous segment;
+ * recv_origin holds (source rank << 28) | the row's sorted position on its source rank.
+ * slot_pos_dev as in ggo_moe_permute. */
 int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int num_experts,
                     int top_k, const int32_t* topk_ids_dev, const void* scratch_dev,
                     const int64_t* counts_all_dev, int world_size, int rank,
@@ -213,9 +214,9 @@ int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int n
 
 /* Grouped GEMM over a receive buffer of capacity_rows rows whose segment counts (device) may sum
  * to less. swiglu != 0: the gate/up SwiGLU form (N = F, weights [E, 2F, K]). With origin_dev set
- * (scatter epilogue), row r's result is stored to peer_out[(segment of r) / num_experts] +
- * origin_dev[r] * N, i.e. straight back to the source rank's buffer over NVLink, and
- * output_dev may be NULL. world_size = number of peer_out entries. */
+ * (scatter epilogue), row r's result is stored to peer_out[origin_dev[r] >> 28] +
+ * (origin_dev[r] & 0x0fffffff) * N, i.e. straight back to the source rank's buffer over
+ * NVLink, and output_dev may be NULL. world_size = number of peer_out entries. */
 int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,
                         const int64_t* tokens_per_segment_dev, int num_segments, int num_experts,
                         int64_t capacity_rows, int64_t N, int64_t K, int dtype, int swiglu,
