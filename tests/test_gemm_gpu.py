@@ -318,3 +318,23 @@ def test_split_tail_launch(ggo, split, monkeypatch):
     ref = oracle.sequential_gemm(x, w, tpe)
     out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), 3)
     assert_parity(out, ref, f"split={split}")
+
+
+@pytest.mark.parametrize("tc", [1, 3])
+def test_dgrad_wgrad_fp16(tc):
+    from grouped_gemm_opt import _C
+    g = torch.Generator().manual_seed(tc)
+    counts = [700, 0, 300, 1100, 20]
+    tpe = torch.tensor(counts)
+    T, n, k = int(tpe.sum()), 256, 512
+    dy = torch.randn(T, n, generator=g).to(torch.float16)
+    x = torch.randn(T, k, generator=g).to(torch.float16)
+    w = (torch.randn(len(counts), n, k, generator=g) * 0.05).to(torch.float16)
+    dx = _C.grouped_gemm_dgrad(dy.to(DEV), w.to(DEV), tpe.to(DEV), tc, True)
+    assert dx.dtype == torch.float16
+    assert_parity(dx, oracle.sequential_gemm(dy, w.transpose(1, 2).contiguous(), tpe), "dgrad fp16")
+    dw = _C.grouped_gemm_wgrad(x.to(DEV), dy.to(DEV), tpe.to(DEV), True)
+    ref = _wgrad_ref(x, dy, tpe)
+    for e, m in enumerate(counts):
+        if m:
+            assert_parity(dw[e], ref[e], f"wgrad fp16 {e}")

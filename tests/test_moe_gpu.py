@@ -130,3 +130,17 @@ def test_swiglu_pair_tile_widths(C, bn, monkeypatch):
     ref = oracle.swiglu_gemm(x, w, tpe, 3)
     h = C.grouped_gemm_swiglu(x.to(DEV), w.to(DEV), tpe.to(DEV), 3, True)
     assert_parity(h, ref, f"swiglu pair bn={bn}")
+
+
+def test_fused_moe_fp16():
+    from grouped_gemm_opt import fused_moe
+    g = torch.Generator().manual_seed(5)
+    T, H, F, E, k = 300, 256, 384, 8, 2
+    x = torch.randn(T, H, generator=g).to(torch.float16)
+    logits = torch.randn(T, E, generator=g)
+    wgu = (torch.randn(E, 2 * F, H, generator=g) * 0.02).to(torch.float16)
+    wd = (torch.randn(E, H, F, generator=g) * 0.02).to(torch.float16)
+    out = fused_moe(x.to(DEV), logits.to(DEV), wgu.to(DEV), wd.to(DEV), k)
+    assert out.dtype == torch.float16
+    ref = oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.float16)
+    assert_parity(out, ref, "fused_moe fp16")
