@@ -14,10 +14,15 @@
 //    W viewed as [E*N, K] serve every segment. Rows of a tile past its segment's end are loaded
 //    (they belong to the next segment or are TMA zero-fill) and masked at the store.
 //  * Warp specialisation: warp 0 = TMA producer, warp 1 = single-thread tcgen05.mma issuer,
-//    warp 2 = TMEM allocator, warps 4..7 = epilogue (TMEM -> registers -> bf16 global stores).
+//    warp 2 = TMEM allocator, warps 4..7 = epilogue (TMEM -> registers -> shared-memory staging
+//    -> TMA stores; masked 16-byte stores where a warp's rows cross a segment boundary).
 //    Two TMEM accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
-//  * Epilogues: plain store, or SwiGLU (silu(gate) * up) for the fused-MoE gate/up projection,
-//    where one 256-wide B tile holds 128 gate rows and the matching 128 up rows.
+//  * Epilogues: plain store; SwiGLU (silu(gate) * up) for the fused-MoE gate/up projection, where
+//    one 256-wide B tile holds 128 gate rows and the matching 128 up rows; row/column-scaled for
+//    FP8 operands; and a scatter of each row to its source rank's buffer (expert parallelism).
+//  * Operand forms: K-major weights (forward), MN-major weights read in place (dgrad), bf16/fp16
+//    (kind::f16) or e4m3 (kind::f8f6f4).
+//  * The CTA-pair variant (ggo_gemm_pair.cuh) shares the segment table, tile decode and epilogue.
 //
 // Every bulk-tensor load writes only the issuing CTA's shared memory, from this GPU's memory.
 #pragma once

@@ -14,10 +14,12 @@ from grouped_gemm_opt._native import _C
 class TileConfig(IntEnum):
     """Tile configuration, value-compatible with the reference enum (ops.py:8-29).
 
-    On B200 the kernel is always the persistent tcgen05 grouped GEMM; the value picks its tile:
-      Co_128x128x64 / PP_128x128x128 -- 128x128 output tile, 6-stage TMA ring
-      Co_128x256x64 / PP_128x256x64  -- 128x256 output tile, 4-stage TMA ring
-      AUTO        -- 128x256 unless that leaves SMs idle (or N <= 128), then 128x128
+    On B200 the kernel is always a persistent tcgen05 grouped GEMM; the value picks its tile:
+      Co_128x128x64 / PP_128x128x128 -- single-CTA 128x128 tile, 6-stage TMA ring
+      Co_128x256x64  -- single-CTA 128x256 tile, 4-stage ring
+      PP_128x256x64  -- CTA pair (cta_group::2), 256x256 tile (+ a pass over short tails)
+      AUTO        -- 128x128 when wider tiles leave SMs idle, the CTA pair when segments
+                     average >= 192 rows, else 128x256 (decided without reading the counts)
       CuBLAS_Seq  -- accepted for compatibility; runs the AUTO choice (no library GEMM)
     """
     Co_128x128x64 = 0

@@ -46,11 +46,13 @@ extern "C" {
 
 /* TileConfig values, identical to the reference enum (csrc/grouped_gemm.h:8-19,
  * grouped_gemm_opt/ops.py:23-28). On sm_100a they select:
- *   0 Co_128x128x64  -> 128x128 tcgen05 tile, 6-stage TMA ring
- *   1 Co_128x256x64  -> 128x256 tcgen05 tile, 4-stage TMA ring
- *   2 PP_128x128x128 -> 128x128 tile (as 0)
- *   3 PP_128x256x64  -> 128x256 tile (as 1)
- *   4 AUTO           -> device-free heuristic on N
+ *   0 Co_128x128x64  -> single-CTA 128x128 tcgen05 tile, 6-stage TMA ring
+ *   1 Co_128x256x64  -> single-CTA 128x256 tile, 4-stage ring
+ *   2 PP_128x128x128 -> single-CTA 128x128 tile (as 0)
+ *   3 PP_128x256x64  -> CTA pair (cta_group::2), 256x256 tile, 6-stage ring, plus a single-CTA
+ *                       pass over short segment tails when they fill two waves
+ *   4 AUTO           -> device-free choice: 128x128 when wider tiles leave SMs idle, the CTA pair
+ *                       when segments average >= 192 rows, else 128x256
  *   5 CuBLAS_Seq     -> accepted for API compatibility; runs the AUTO choice (no library GEMM) */
 #define GGO_TILE_CO_128x128x64 0
 #define GGO_TILE_CO_128x256x64 1
