@@ -614,6 +614,10 @@ int ggo_ipc_close(void* peer_ptr) {
 
 int ggo_ipc_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? GGO_OK : GGO_ERR_CUDA; }
 
+uint64_t ggo_kernel_launches(void) {
+  return ggo::g_kernel_launches.load(std::memory_order_relaxed);
+}
+
 const char* ggo_last_cuda_error_string(void) {
   const int c = ggo::g_last_cuda_error;
   if (c == 0) return "no CUDA error recorded";

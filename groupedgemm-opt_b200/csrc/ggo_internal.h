@@ -3,6 +3,9 @@
 
 #include "ggo.h"
 
+#include <atomic>
+#include <cstdint>
+
 #include <cuda_runtime_api.h>
 
 namespace ggo {
@@ -16,7 +19,12 @@ inline int cuda_fail(int code) {
   return GGO_ERR_CUDA;
 }
 
+// Kernels launched by this library in this process (ggo_kernel_launches()).
+inline std::atomic<uint64_t> g_kernel_launches{0};
+
+// Called right after every kernel launch.
 inline int check_launch() {
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GGO_OK : cuda_fail(static_cast<int>(e));
 }

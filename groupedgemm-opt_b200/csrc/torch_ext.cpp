@@ -513,6 +513,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("slot_pos"));
   m.def("workspace_error", &workspace_error, py::arg("device") = 0);
   m.def("abi_version", []() { return ggo_version(); });
+  m.def("kernel_launches", []() { return static_cast<int64_t>(ggo_kernel_launches()); });
   m.def("grouped_gemm_host", &grouped_gemm_host, py::arg("input"), py::arg("weights"),
         py::arg("tokens_per_expert"), py::arg("out"), py::arg("tile_config") = 4,
         py::arg("sort_by_m") = true, py::arg("chunks") = 4);

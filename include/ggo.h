@@ -64,6 +64,9 @@ extern "C" {
 /* After a call returned GGO_ERR_CUDA: the CUDA error it met, as text (this thread's last). */
 const char* ggo_last_cuda_error_string(void);
 
+/* Number of kernels this library has launched in this process (for launch accounting). */
+uint64_t ggo_kernel_launches(void);
+
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int ggo_version(void);
 

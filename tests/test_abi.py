@@ -38,6 +38,8 @@ def test_metadata_calls(lib):
         assert lib.ggo_status_string(code)
     lib.ggo_workspace_size.restype = ctypes.c_size_t
     assert lib.ggo_workspace_size() == 256
+    lib.ggo_kernel_launches.restype = ctypes.c_uint64
+    assert lib.ggo_kernel_launches() >= 0
     lib.ggo_moe_route_scratch_bytes.restype = ctypes.c_size_t
     lib.ggo_moe_route_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int]
     assert lib.ggo_moe_route_scratch_bytes(16384, 8) == (16384 // 32 + 1) * 8 * 4
