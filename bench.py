@@ -550,6 +550,8 @@ def main():
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": UNIT, "frac": achieved / peak,
                          "peak_source": f"{peak_src} bf16_tflops_sustained (of {peak_src})",
+                         "kernel": "grouped_gemm_pair_kernel (+ its short-tail pass, "
+                                   "empty for uniform routing), device time per step",
                          "traffic": traffic},
             "clocks": clocks,
             "gpu_launches": launches,
