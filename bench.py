@@ -255,6 +255,19 @@ def moe_layer_bench(world, rank, steps, warmup):
            "kernels_per_step": 6}
     if world > 1:
         out["nccl_all_to_all_value"] = T / (res["nccl"] / 1e3)
+    # Roofline of the layer on each rank: the slower of its FLOPs at the measured sustained bf16
+    # peak and the bytes it must move over NVLink (rows sent to other ranks and results sent back,
+    # per direction) at the measured 770 GB/s peer copy rate.
+    peaks, src = _peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1590.0)))
+    t_flop = flops / world / (peak * 1e12) * 1e3
+    nvl_bytes = 2.0 * tl * k * H * 2 * (world - 1) / world
+    t_nvl = nvl_bytes / 770e9 * 1e3
+    target = max(t_flop, t_nvl)
+    out["roofline"] = {"bound": "tensor" if t_flop >= t_nvl else "nvlink", "target_ms": target,
+                       "achieved_ms": ms, "frac": target / ms,
+                       "peak": f"{peak} TFLOP/s bf16 sustained ({src}), 770 GB/s NVLink",
+                       "nvlink_bytes_per_gpu_per_direction": nvl_bytes}
     return out
 
 
