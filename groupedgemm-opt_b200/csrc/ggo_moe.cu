@@ -339,6 +339,64 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------------------------------------------------------- expert-parallel signalling
+// Each rank owns an IPC-shared sync board: counts [kMaxPeers][E] int64 (every rank's
+// tokens_per_expert, written by that rank) and flags [kEpSlots][kMaxPeers] int64 (per phase, the
+// last layer epoch each rank has completed). A rank posts by storing into every peer's board;
+// a rank waits by polling its own board. Epochs only grow, so no reset is needed.
+constexpr int kEpSlots = 4;
+
+struct PeerBoards {
+  int64_t* board[kMaxPeers];
+};
+
+// Stores this rank's tokens_per_expert into row `rank` of every peer's counts board, then (after a
+// system-scope fence) its epoch into every peer's flags[slot][rank]. One block.
+__global__ void ep_publish_counts_kernel(const int64_t* __restrict__ tpe, PeerBoards pb, int world,
+                                         int rank, int E, int slot, long long epoch) {
+  for (int r = 0; r < world; ++r)
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      pb.board[r][static_cast<size_t>(rank) * E + e] = tpe[e];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world) {
+    volatile long long* f = reinterpret_cast<volatile long long*>(
+        pb.board[threadIdx.x] + static_cast<size_t>(kMaxPeers) * E + slot * kMaxPeers + rank);
+    *f = epoch;
+  }
+}
+
+// After the previous kernels on this stream (which fenced their peer stores), tells every peer
+// that this rank finished phase `slot` of layer `epoch`.
+__global__ void ep_signal_kernel(PeerBoards pb, int world, int rank, int E, int slot,
+                                 long long epoch) {
+  __threadfence_system();
+  if (threadIdx.x < world) {
+    volatile long long* f = reinterpret_cast<volatile long long*>(
+        pb.board[threadIdx.x] + static_cast<size_t>(kMaxPeers) * E + slot * kMaxPeers + rank);
+    *f = epoch;
+  }
+}
+
+// Waits until every rank has posted `epoch` for `slot` in this rank's own board. Bounded: after
+// `limit` cycles it records kErrEpTimeout in *err and returns (the data of the phase is then
+// incomplete and the host reports the error).
+__global__ void ep_wait_kernel(const int64_t* __restrict__ own_board, int world, int E, int slot,
+                               long long epoch, int* err, long long limit) {
+  if (threadIdx.x < world) {
+    const volatile long long* f = reinterpret_cast<const volatile long long*>(
+        own_board + static_cast<size_t>(kMaxPeers) * E + slot * kMaxPeers + threadIdx.x);
+    const long long t0 = clock64();
+    while (*f < epoch) {
+      if (clock64() - t0 > limit) {
+        atomicCAS(err, 0, 104);  // device error code: expert-parallel peer wait timed out
+        break;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int nblocks_for(int64_t T) { return static_cast<int>((T + kRouteTokens - 1) / kRouteTokens); }
@@ -467,6 +525,53 @@ int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dty
     ggo::quantize_rows_fp8_kernel<__half><<<grid, 256, 0, stream>>>(
         static_cast<const __half*>(x_dev), static_cast<int>(rows), static_cast<int>(cols),
         static_cast<uint8_t*>(q_dev), scale_dev);
+  return ggo::check_launch();
+}
+
+size_t ggo_ep_board_bytes(int num_experts) {
+  return (static_cast<size_t>(ggo::kMaxPeers) * num_experts +
+          static_cast<size_t>(ggo::kEpSlots) * ggo::kMaxPeers) * sizeof(int64_t);
+}
+
+static int ep_boards(int64_t* const* boards, int world, ggo::PeerBoards* pb) {
+  if (!boards || world < 1 || world > ggo::kMaxPeers) return GGO_ERR_INVALID_ARG;
+  for (int r = 0; r < ggo::kMaxPeers; ++r) pb->board[r] = r < world ? boards[r] : nullptr;
+  for (int r = 0; r < world; ++r)
+    if (!boards[r]) return GGO_ERR_INVALID_ARG;
+  return GGO_OK;
+}
+
+int ggo_ep_publish_counts(const int64_t* tokens_per_expert_dev, int64_t* const* boards,
+                          int world_size, int rank, int num_experts, int slot, int64_t epoch,
+                          cudaStream_t stream) {
+  ggo::PeerBoards pb;
+  if (int st = ep_boards(boards, world_size, &pb)) return st;
+  if (!tokens_per_expert_dev || rank < 0 || rank >= world_size || num_experts <= 0 || slot < 0 ||
+      slot >= ggo::kEpSlots)
+    return GGO_ERR_INVALID_ARG;
+  ggo::ep_publish_counts_kernel<<<1, 256, 0, stream>>>(tokens_per_expert_dev, pb, world_size,
+                                                        rank, num_experts, slot, epoch);
+  return ggo::check_launch();
+}
+
+int ggo_ep_signal(int64_t* const* boards, int world_size, int rank, int num_experts, int slot,
+                  int64_t epoch, cudaStream_t stream) {
+  ggo::PeerBoards pb;
+  if (int st = ep_boards(boards, world_size, &pb)) return st;
+  if (rank < 0 || rank >= world_size || num_experts <= 0 || slot < 0 || slot >= ggo::kEpSlots)
+    return GGO_ERR_INVALID_ARG;
+  ggo::ep_signal_kernel<<<1, 32, 0, stream>>>(pb, world_size, rank, num_experts, slot, epoch);
+  return ggo::check_launch();
+}
+
+int ggo_ep_wait(const int64_t* own_board, int world_size, int num_experts, int slot,
+                int64_t epoch, void* workspace_dev, int64_t limit_cycles, cudaStream_t stream) {
+  if (!own_board || !workspace_dev || world_size < 1 || world_size > ggo::kMaxPeers ||
+      num_experts <= 0 || slot < 0 || slot >= ggo::kEpSlots || limit_cycles <= 0)
+    return GGO_ERR_INVALID_ARG;
+  int* err = static_cast<int*>(workspace_dev) + 2;  // GgoWorkspace::error
+  ggo::ep_wait_kernel<<<1, 32, 0, stream>>>(own_board, world_size, num_experts, slot, epoch, err,
+                                            limit_cycles);
   return ggo::check_launch();
 }
 

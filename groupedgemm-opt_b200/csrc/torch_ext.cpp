@@ -486,6 +486,47 @@ torch::Tensor ep_grouped_gemm(const torch::Tensor& input, const torch::Tensor& w
   return out;
 }
 
+// ------------------------------------------------------------------ EP device-side signalling
+std::vector<int64_t*> board_ptrs(const std::vector<int64_t>& v) {
+  std::vector<int64_t*> out(v.size());
+  for (size_t i = 0; i < v.size(); ++i) out[i] = reinterpret_cast<int64_t*>(v[i]);
+  return out;
+}
+
+void ep_publish_counts(const torch::Tensor& tpe, std::vector<int64_t> boards, int64_t rank,
+                       int64_t slot, int64_t epoch) {
+  TORCH_CHECK(tpe.is_cuda() && tpe.scalar_type() == torch::kInt64 && tpe.is_contiguous(),
+              "tokens_per_expert must be contiguous int64 CUDA");
+  c10::cuda::CUDAGuard guard(tpe.device());
+  auto b = board_ptrs(boards);
+  check_status(ggo_ep_publish_counts(tpe.data_ptr<int64_t>(), b.data(),
+                                     static_cast<int>(b.size()), static_cast<int>(rank),
+                                     static_cast<int>(tpe.numel()), static_cast<int>(slot), epoch,
+                                     at::cuda::getCurrentCUDAStream()),
+               "EP count publish");
+}
+
+void ep_signal(std::vector<int64_t> boards, int64_t rank, int64_t num_experts, int64_t slot,
+               int64_t epoch, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  auto b = board_ptrs(boards);
+  check_status(ggo_ep_signal(b.data(), static_cast<int>(b.size()), static_cast<int>(rank),
+                             static_cast<int>(num_experts), static_cast<int>(slot), epoch,
+                             at::cuda::getCurrentCUDAStream()),
+               "EP signal");
+}
+
+void ep_wait(int64_t own_board, int64_t world, int64_t num_experts, int64_t slot, int64_t epoch,
+             int64_t limit_cycles, int64_t device) {
+  const torch::Device dev(torch::kCUDA, static_cast<c10::DeviceIndex>(device));
+  c10::cuda::CUDAGuard guard(dev);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(ggo_ep_wait(reinterpret_cast<const int64_t*>(own_board), static_cast<int>(world),
+                           static_cast<int>(num_experts), static_cast<int>(slot), epoch,
+                           workspace_for(dev, stream), limit_cycles, stream),
+               "EP wait");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -517,6 +558,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_host", &grouped_gemm_host, py::arg("input"), py::arg("weights"),
         py::arg("tokens_per_expert"), py::arg("out"), py::arg("tile_config") = 4,
         py::arg("sort_by_m") = true, py::arg("chunks") = 4);
+  m.def("ep_board_bytes", [](int64_t e) { return static_cast<int64_t>(ggo_ep_board_bytes(static_cast<int>(e))); });
+  m.def("ep_publish_counts", &ep_publish_counts, py::arg("tokens_per_expert"), py::arg("boards"),
+        py::arg("rank"), py::arg("slot"), py::arg("epoch"));
+  m.def("ep_signal", &ep_signal, py::arg("boards"), py::arg("rank"), py::arg("num_experts"),
+        py::arg("slot"), py::arg("epoch"), py::arg("device"));
+  m.def("ep_wait", &ep_wait, py::arg("own_board"), py::arg("world"), py::arg("num_experts"),
+        py::arg("slot"), py::arg("epoch"), py::arg("limit_cycles"), py::arg("device"));
   m.def("ipc_alloc", &ipc_alloc, py::arg("nbytes"));
   m.def("ipc_open", &ipc_open, py::arg("handle"));
   m.def("ipc_close", &ipc_close, py::arg("ptr"));

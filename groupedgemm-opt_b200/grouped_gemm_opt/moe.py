@@ -86,13 +86,19 @@ class EPBuffers:
         self.capacity = self.world * max_tokens * top_k
         esz = torch.empty(0, dtype=dtype).element_size()
         sizes = {"recv": self.capacity * hidden * esz, "origin": self.capacity * 4,
-                 "back": max_tokens * top_k * hidden * esz}
+                 "back": max_tokens * top_k * hidden * esz,
+                 "board": int(_C.ep_board_bytes(num_experts))}
         self._own = {}
         handles = {}
         for name, nbytes in sizes.items():
             ptr, h = _C.ipc_alloc(max(nbytes, 256))
             self._own[name] = ptr
             handles[name] = h
+        # the sync board must start at zero (counts and epoch flags) before any peer writes to it
+        dev = self.device.index
+        self._board_elems = int(_C.ep_board_bytes(num_experts)) // 8
+        _C.tensor_view(self._own["board"], [self._board_elems], torch.int64, dev).zero_()
+        torch.cuda.synchronize(self.device)
         gathered = [None] * self.world
         dist.all_gather_object(gathered, handles, group=group)
         self.ptrs = {name: [] for name in sizes}
@@ -110,6 +116,10 @@ class EPBuffers:
         self.origin = _C.tensor_view(self._own["origin"], [self.capacity], torch.int32, dev)
         self.back = _C.tensor_view(self._own["back"], [max_tokens * top_k, hidden], dtype, dev)
         self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # own board: counts rows of every rank (first `world` of 8), then the epoch flags
+        self.board_counts = _C.tensor_view(self._own["board"], [8, num_experts], torch.int64, dev)
+        self.epoch = 0
+        self.wait_limit_cycles = 1 << 34  # ~10 s at 1.9 GHz, then the wait records a timeout
         dist.barrier(group=group)
 
     def fence(self):
@@ -134,7 +144,9 @@ def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuf
                    sort_by_m):
     """Expert-parallel layer over NVLink peer memory: the dispatch kernel writes rows into the
     owners' receive buffers, the down GEMM's epilogue writes results back into the sources'
-    return buffers; two one-element all-reduces order the phases. No host synchronisation."""
+    return buffers. The phases are ordered by device-side epoch flags in the IPC-shared sync
+    boards (post with system-scope stores, bounded waits): no host synchronisation and no
+    NCCL call in the layer."""
     C = bufs._C
     world, rank = bufs.world, bufs.rank
     T, H = hidden.shape
@@ -142,18 +154,27 @@ def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuf
     el = E // world
     assert T <= bufs.max_tokens and H == bufs.hidden and top_k == bufs.top_k, "EPBuffers too small"
     assert E == bufs.num_experts and hidden.dtype == bufs.dtype
+    bufs.epoch += 1
+    ep, dev, boards, own = bufs.epoch, hidden.device.index, bufs.ptrs["board"], bufs._own["board"]
+    lim = bufs.wait_limit_cycles
     ids, w, tpe, scratch = C.moe_route(router_logits, top_k)
-    counts_all = torch.empty(world, E, dtype=torch.int64, device=hidden.device)
-    dist.all_gather_into_tensor(counts_all, tpe, group=bufs.group)
+    # phase 0: every rank's counts land in every board
+    C.ep_publish_counts(tpe, boards, rank, 0, ep)
+    C.ep_wait(own, world, E, 0, ep, lim, dev)
+    counts_all = bufs.board_counts[:world]
     slot_pos = C.ep_dispatch(hidden, ids, scratch, counts_all, rank, bufs.ptrs["recv"],
                              bufs.ptrs["origin"])
-    bufs.fence()
+    # phase 1: every source has delivered its rows to this rank
+    C.ep_signal(boards, rank, E, 1, ep, dev)
+    C.ep_wait(own, world, E, 1, ep, lim, dev)
     # receive buffer is expert-major: one segment per local expert, rows from every source
     seg_counts = counts_all[:, rank * el:(rank + 1) * el].sum(0)
     h = C.ep_grouped_gemm(bufs.recv, w_gate_up, seg_counts, el, True, None, [], sort_by_m)
     C.ep_grouped_gemm(h, w_down, seg_counts, el, False, bufs.origin, bufs.ptrs["back"],
                       sort_by_m)
-    bufs.fence()
+    # phase 2: every owner has scattered this rank's results back
+    C.ep_signal(boards, rank, E, 2, ep, dev)
+    C.ep_wait(own, world, E, 2, ep, lim, dev)
     return C.moe_combine(bufs.back[:T * top_k], w, slot_pos)
 
 

@@ -217,6 +217,27 @@ int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int n
                     void* const* recv_rows, int32_t* const* recv_origin, int32_t* slot_pos_dev,
                     int dtype, cudaStream_t stream);
 
+/* Device-side signalling between the ranks of the fused expert-parallel path, replacing host
+ * collectives. Every rank allocates a sync board of ggo_ep_board_bytes(E) bytes (zero-filled,
+ * IPC-shared): counts [8][E] int64 (row r = rank r's tokens_per_expert) and flags [4][8] int64
+ * (per phase slot, the last epoch each rank completed). boards[r] = rank r's board as mapped here.
+ * Epochs must grow from layer to layer (start at 1).
+ *   ggo_ep_publish_counts: write this rank's tokens_per_expert into every board, then post
+ *                          `epoch` for `slot`.
+ *   ggo_ep_signal:         post `epoch` for `slot` (after the peer stores of earlier kernels on
+ *                          `stream`, which must end with a system-scope fence).
+ *   ggo_ep_wait:           wait until every rank posted `epoch` for `slot` on this rank's board;
+ *                          bounded by limit_cycles (SM clock), after which the workspace error
+ *                          word records GGO_ERR_DEVICE_TIMEOUT (read it with ggo_workspace_error). */
+size_t ggo_ep_board_bytes(int num_experts);
+int ggo_ep_publish_counts(const int64_t* tokens_per_expert_dev, int64_t* const* boards,
+                          int world_size, int rank, int num_experts, int slot, int64_t epoch,
+                          cudaStream_t stream);
+int ggo_ep_signal(int64_t* const* boards, int world_size, int rank, int num_experts, int slot,
+                  int64_t epoch, cudaStream_t stream);
+int ggo_ep_wait(const int64_t* own_board, int world_size, int num_experts, int slot,
+                int64_t epoch, void* workspace_dev, int64_t limit_cycles, cudaStream_t stream);
+
 /* Grouped GEMM over a receive buffer of capacity_rows rows whose segment counts (device) may sum
  * to less. swiglu != 0: the gate/up SwiGLU form (N = F, weights [E, 2F, K]). With origin_dev set
  * (scatter epilogue), row r's result is stored to peer_out[origin_dev[r] >> 28] +
