@@ -33,3 +33,22 @@ def test_bounded_wait_times_out_and_recovers(tc, monkeypatch):
     torch.cuda.synchronize()
     ggo.check_device_errors(0)
     assert_parity(out, oracle.sequential_gemm(x, w, tpe), f"after timeout tc={tc}")
+
+
+def test_ep_peer_wait_times_out_then_succeeds():
+    """The expert-parallel peer wait on one GPU: an epoch nobody posted makes the bounded wait
+    expire (recorded as GGO_ERR_DEVICE_TIMEOUT), a posted one passes."""
+    import grouped_gemm_opt as ggo
+    from grouped_gemm_opt import _C
+    E = 8
+    board = torch.zeros(_C.ep_board_bytes(E) // 8, dtype=torch.int64, device=DEV)
+    ggo.check_device_errors(0)
+    _C.ep_wait(board.data_ptr(), 1, E, 3, 1, 1 << 24, 0)  # nothing posted epoch 1 for slot 3
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="error code 8$"):
+        ggo.check_device_errors(0)
+    _C.ep_signal([board.data_ptr()], 0, E, 3, 1, 0)
+    _C.ep_wait(board.data_ptr(), 1, E, 3, 1, 1 << 24, 0)
+    torch.cuda.synchronize()
+    ggo.check_device_errors(0)
+    assert int(board[8 * E + 3 * 8 + 0]) == 1  # flags[slot 3][rank 0]
