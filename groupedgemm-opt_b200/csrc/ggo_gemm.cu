@@ -140,7 +140,7 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   constexpr int smem = SmemLayout<BN>::kTotal;
   int sms = 0;
   if (int st = kernel_setup(kern, smem, dev, false, &sms)) return st;
-  constexpr int out_bn = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  constexpr int out_bn = epi_glu(EPI) ? BN / 2 : BN;
   const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
   const int64_t ub = ((p.rows + kBM - 1) / kBM + p.num_segments) * n_tiles;  // tile upper bound
   const int grid = static_cast<int>(ub < sms ? ub : sms);
@@ -166,7 +166,7 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
   constexpr int smem = PairLayout<BN>::kTotal;
   int clusters = 0;
   if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
-  constexpr int out_bn = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  constexpr int out_bn = epi_glu(EPI) ? BN / 2 : BN;
   const int64_t n_tiles = (p.n_out + out_bn - 1) / out_bn;
   const int64_t ub = ((p.rows + 255) / 256 + p.num_segments) * n_tiles;  // pair-tile upper bound
   const int64_t pairs = ub < clusters ? ub : clusters;
@@ -287,7 +287,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   if (num_segments > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
   const bool fp8 = ex && ex->fp8;
   if (fp8) {
-    if (!ex->row_scale || !ex->col_scale || swiglu || bmn || scatter) return GGO_ERR_INVALID_ARG;
+    if (!ex->row_scale || !ex->col_scale || bmn || scatter) return GGO_ERR_INVALID_ARG;
     dtype = GGO_DTYPE_BF16;  // e4m3 in, bf16 out
     if (k % 16) return GGO_ERR_ALIGNMENT;  // rows of K bytes must be 16-byte multiples
   }
@@ -333,18 +333,24 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   if (fp8) {  // CTA-pair pass (+ short-tail pass) or single-CTA 128x256, scaled epilogue
     if (bn == 512) {
       const bool split = env_int("GGO_SPLIT_TAILS", 1) > 0;
-      p.split_tail_ntiles = static_cast<int>((n + 255) / 256);
+      p.split_tail_ntiles = static_cast<int>((n + (swiglu ? 127 : 255)) / (swiglu ? 128 : 256));
       p.split_min_tiles = env_int("GGO_SPLIT_MIN_TILES", 2 * g_sm_count[dev]);
       GemmParams pp = p;
       pp.group_m = raster_group_m(k / 2, 256);  // k bytes: half the bf16 panel size
       pp.split_mode = split ? 1 : 0;
-      if (int st = launch_pair<256, kEpiScaled, true, false, true>(input, weights, b_rows, pp,
-                                                                   dev, stream))
-        return st;
+      const int st =
+          swiglu ? launch_pair<256, kEpiScaledSwiGLU, true, false, true>(input, weights, b_rows,
+                                                                         pp, dev, stream)
+                 : launch_pair<256, kEpiScaled, true, false, true>(input, weights, b_rows, pp, dev,
+                                                                   stream);
+      if (st) return st;
       if (!split) return GGO_OK;
       p.split_mode = 2;
     }
-    return launch<256, kEpiScaled, true, false, true>(input, weights, b_rows, p, dev, stream);
+    return swiglu
+               ? launch<256, kEpiScaledSwiGLU, true, false, true>(input, weights, b_rows, p, dev,
+                                                                  stream)
+               : launch<256, kEpiScaled, true, false, true>(input, weights, b_rows, p, dev, stream);
   }
   if (bn == 512) {
     // CTA-pair pass over 256-row tiles, then (GGO_SPLIT_TAILS, default on) a single-CTA pass over
@@ -566,6 +572,20 @@ int ggo_grouped_gemm_fp8(const void* input_dev, const float* input_scale_dev,
   return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_expert_dev, num_experts,
                           num_experts, total_tokens, N, K, GGO_DTYPE_BF16, tile_config, sort_by_m,
                           workspace_dev, stream, false, &ex);
+}
+
+int ggo_grouped_gemm_swiglu_fp8(const void* x_dev, const float* x_scale_dev,
+                                const void* w_gate_up_dev, const float* w_scale_dev, void* h_dev,
+                                const int64_t* tokens_per_segment_dev, int num_segments,
+                                int num_experts, int64_t total_tokens, int64_t F, int64_t K,
+                                int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  ggo::GemmExtras ex;
+  ex.fp8 = 1;
+  ex.row_scale = x_scale_dev;
+  ex.col_scale = w_scale_dev;
+  return ggo::gemm_common(x_dev, w_gate_up_dev, h_dev, tokens_per_segment_dev, num_segments,
+                          num_experts, total_tokens, F, K, GGO_DTYPE_BF16, GGO_TILE_AUTO,
+                          sort_by_m, workspace_dev, stream, true, &ex);
 }
 
 int ggo_ep_grouped_gemm(const void* input_dev, const void* weights_dev, void* output_dev,

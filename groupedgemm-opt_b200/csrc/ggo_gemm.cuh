@@ -44,7 +44,13 @@ constexpr int kSchedDepth = 4;
 constexpr int kThreads = 256;
 
 // kEpiScaled: out = acc * row_scale[row] * col_scale[expert * n_out + col] (the FP8 path).
-enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScaled = 2 };
+// kEpiScaledSwiGLU: silu(gate * rs * cs_gate) * (up * rs * cs_up) (the FP8 gate/up projection).
+enum EpiKind { kEpiStore = 0, kEpiSwiGLU = 1, kEpiScaled = 2, kEpiScaledSwiGLU = 3 };
+
+// Epilogues whose B tile is [gate rows | up rows] and whose output is half the tile width.
+__host__ __device__ constexpr bool epi_glu(int e) {
+  return e == kEpiSwiGLU || e == kEpiScaledSwiGLU;
+}
 
 // Error codes written to GgoWorkspace::error (first error wins).
 enum DevError {
@@ -303,7 +309,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     // MN-major weights [E, Kred, n_out]: rows are the reduction index; the column is n0
     info.brow0 = expert * p.k;
     info.brow1 = info.brow0;
-  } else if (EPI == kEpiSwiGLU) {
+  } else if (epi_glu(EPI)) {
     info.brow0 = expert * p.n_b + info.n0;                 // gate rows
     info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows
   } else {
@@ -326,8 +332,27 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 // columns [c, c+32) (plain), or silu(gate) * up from columns [c, c+32) and [BN/2 + c, ...).
 template <int BN, int EPI, bool BF16>
 __device__ __forceinline__ void load_out32(uint32_t t_row, int c, uint32_t (&o)[16], float rs = 1.f,
-                                           const float* cs = nullptr, int cs_valid = 0) {
-  if (EPI == kEpiScaled) {
+                                           const float* cs = nullptr, int cs_valid = 0,
+                                           int cs_up_off = 0) {
+  if (EPI == kEpiScaledSwiGLU) {
+    uint32_t g[32], u[32];
+    tmem_ld_32x32b_x32(t_row + c, g);
+    tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float y[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * i + e;
+        const bool ok = j < cs_valid;
+        const float gv = __uint_as_float(g[j]) * rs * (ok ? __ldg(cs + j) : 0.f);
+        const float uv = __uint_as_float(u[j]) * rs * (ok ? __ldg(cs + cs_up_off + j) : 0.f);
+        y[e] = gv / (1.0f + __expf(-gv)) * uv;
+      }
+      o[i] = pack2(y[0], y[1], BF16);
+    }
+  } else if (EPI == kEpiScaled) {
     uint32_t v[32];
     tmem_ld_32x32b_x32(t_row + c, v);
     tmem_ld_wait();
@@ -378,8 +403,9 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
                                                 OutT* out_row, bool warp_tma,
                                                 const CUtensorMap* tmC, uint8_t* stage,
                                                 int x_row0, float rs = 1.f,
-                                                const float* cs_row = nullptr) {
-  constexpr int OUTW = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+                                                const float* cs_row = nullptr,
+                                                int cs_up_off = 0) {
+  constexpr int OUTW = epi_glu(EPI) ? BN / 2 : BN;
   const int lane = threadIdx.x & 31;
   const uint32_t st_row = smem_u32(stage) + lane * 128;
 #pragma unroll 1
@@ -394,7 +420,7 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
       if (c >= OUTW) break;
       uint32_t o[16];
       load_out32<BN, EPI, BF16>(t_row, c, o, rs, cs_row ? cs_row + n0 + c : nullptr,
-                                n_out - (n0 + c));
+                                n_out - (n0 + c), cs_up_off);
       if (warp_tma) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -443,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = SmemLayout<BN>;
   constexpr int S = L::kStages;
   constexpr int kTmemCols = 2 * BN;             // two accumulators
-  constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  constexpr int kOutBN = epi_glu(EPI) ? BN / 2 : BN;
   constexpr bool kTmaStoreOk = kOutBN % 64 == 0;  // output boxes are 64 columns wide
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -620,12 +646,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       const bool warp_tma = kTmaStoreOk && p.use_tma_store && ew * 32 + 32 <= info.rows;
-      const float rs = (EPI == kEpiScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
-      const float* cs_row = EPI == kEpiScaled
-                                ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_out
-                                : nullptr;
+      constexpr bool kScaled = EPI == kEpiScaled || EPI == kEpiScaledSwiGLU;
+      const float rs = (kScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
+      // column scales: one per weight row, [E, n_b] (gate rows then up rows for SwiGLU)
+      const float* cs_row =
+          kScaled ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_b : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
-                                     staging + ew * 4096, info.row0 + ew * 32, rs, cs_row);
+                                     staging + ew * 4096, info.row0 + ew * 32, rs, cs_row,
+                                     p.n_b / 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);

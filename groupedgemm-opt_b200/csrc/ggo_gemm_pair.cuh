@@ -246,12 +246,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       const int wrow0 = static_cast<int>(rank) * 128 + ew * 32;
       const bool warp_tma = kTmaStoreOk && p.use_tma_store && wrow0 + 32 <= info.rows;
-      const float rs = (EPI == kEpiScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
-      const float* cs_row = EPI == kEpiScaled
-                                ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_out
-                                : nullptr;
+      constexpr bool kScaled = EPI == kEpiScaled || EPI == kEpiScaledSwiGLU;
+      const float rs = (kScaled && row_ok) ? __ldg(p.row_scale + info.row0 + r_local) : 1.f;
+      // column scales: one per weight row, [E, n_b] (gate rows then up rows for SwiGLU)
+      const float* cs_row =
+          kScaled ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_b : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
-                                     staging + ew * 4096, info.row0 + wrow0, rs, cs_row);
+                                     staging + ew * 4096, info.row0 + wrow0, rs, cs_row,
+                                     p.n_b / 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));

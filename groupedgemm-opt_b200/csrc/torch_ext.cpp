@@ -197,6 +197,37 @@ torch::Tensor grouped_gemm_fp8(const torch::Tensor& a_q, const torch::Tensor& a_
   return out;
 }
 
+// FP8 gate/up SwiGLU grouped GEMM: h bf16 [T, F].
+torch::Tensor grouped_gemm_swiglu_fp8(const torch::Tensor& x_q, const torch::Tensor& x_scale,
+                                      const torch::Tensor& w_q, const torch::Tensor& w_scale,
+                                      const torch::Tensor& counts, int64_t num_experts,
+                                      bool sort_by_m) {
+  TORCH_CHECK(x_q.is_cuda() && w_q.is_cuda() && x_q.dim() == 2 && w_q.dim() == 3,
+              "x_q [T, K] and w_q [E, 2F, K] CUDA tensors");
+  TORCH_CHECK(x_q.scalar_type() == torch::kFloat8_e4m3fn &&
+                  w_q.scalar_type() == torch::kFloat8_e4m3fn, "operands must be float8_e4m3fn");
+  TORCH_CHECK(x_q.size(1) == w_q.size(2) && w_q.size(1) % 2 == 0, "shape mismatch");
+  TORCH_CHECK(x_q.is_contiguous() && w_q.is_contiguous(), "operands must be contiguous");
+  TORCH_CHECK(x_scale.scalar_type() == torch::kFloat32 && x_scale.numel() == x_q.size(0) &&
+                  w_scale.scalar_type() == torch::kFloat32 &&
+                  w_scale.numel() == w_q.size(0) * w_q.size(1) && x_scale.is_contiguous() &&
+                  w_scale.is_contiguous(),
+              "scales: fp32 [T] and [E, 2F]");
+  c10::cuda::CUDAGuard guard(x_q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x_q.size(0), K = x_q.size(1), F = w_q.size(1) / 2;
+  auto h = torch::empty({T, F}, x_q.options().dtype(torch::kBFloat16));
+  if (T == 0) return h;
+  auto c = counts_on_device(counts, x_q.device());
+  const int st = ggo_grouped_gemm_swiglu_fp8(
+      x_q.data_ptr(), x_scale.data_ptr<float>(), w_q.data_ptr(), w_scale.data_ptr<float>(),
+      h.data_ptr(), c.data_ptr<int64_t>(), static_cast<int>(c.size(0)),
+      static_cast<int>(num_experts), T, F, K, sort_by_m ? 1 : 0,
+      workspace_for(x_q.device(), stream), stream);
+  check_status(st, "fp8 gate/up SwiGLU grouped GEMM");
+  return h;
+}
+
 torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
                                   const torch::Tensor& counts, int64_t num_experts,
                                   bool sort_by_m) {
@@ -542,6 +573,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_wgrad", &grouped_gemm_wgrad, py::arg("x"), py::arg("dy"),
         py::arg("tokens_per_expert"), py::arg("sort_by_m") = true);
   m.def("quantize_fp8_rows", &quantize_fp8_rows, py::arg("x"));
+  m.def("grouped_gemm_swiglu_fp8", &grouped_gemm_swiglu_fp8, py::arg("x_q"), py::arg("x_scale"),
+        py::arg("w_gate_up_q"), py::arg("w_scale"), py::arg("tokens_per_segment"),
+        py::arg("num_experts"), py::arg("sort_by_m") = true);
   m.def("grouped_gemm_fp8", &grouped_gemm_fp8, py::arg("input_q"), py::arg("input_scale"),
         py::arg("weights_q"), py::arg("weight_scale"), py::arg("tokens_per_expert"),
         py::arg("tile_config") = 4, py::arg("sort_by_m") = true);

@@ -6,8 +6,10 @@ from grouped_gemm_opt.ops import (TileConfig, check_device_errors, grouped_gemm_
                                   grouped_gemm_opt_fp8, grouped_gemm_opt_host, quantize_fp8)
 from grouped_gemm_opt.triton_fused_moe import triton_fused_moe
 from grouped_gemm_opt.triton_grouped_gemm import triton_grouped_gemm
-from grouped_gemm_opt.moe import EPBuffers, fused_moe
+from grouped_gemm_opt.moe import (EPBuffers, MoEFP8Weights, fused_moe, fused_moe_fp8,
+                                  quantize_moe_weights)
 
 __all__ = ["grouped_gemm_opt", "TileConfig", "triton_fused_moe", "triton_grouped_gemm",
            "fused_moe", "check_device_errors", "grouped_gemm_opt_host", "EPBuffers",
-           "grouped_gemm_opt_fp8", "quantize_fp8"]
+           "grouped_gemm_opt_fp8", "quantize_fp8", "fused_moe_fp8", "quantize_moe_weights",
+           "MoEFP8Weights"]

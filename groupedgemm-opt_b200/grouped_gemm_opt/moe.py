@@ -251,3 +251,39 @@ def fused_moe(
     y_back = y.new_empty((xs.size(0), H))
     dist.all_to_all_single(y_back, y, send_splits, recv_splits, group=ep_group)
     return ops.combine(y_back, w, slot_pos)
+
+
+@dataclass
+class MoEFP8Weights:
+    """e4m3 expert weights with one fp32 scale per output channel (see quantize_moe_weights)."""
+    w_gate_up_q: torch.Tensor      # [E, 2F, H] float8_e4m3fn
+    w_gate_up_scale: torch.Tensor  # [E, 2F] fp32
+    w_down_q: torch.Tensor         # [E, H, F] float8_e4m3fn
+    w_down_scale: torch.Tensor     # [E, H] fp32
+
+
+def quantize_moe_weights(w_gate_up: torch.Tensor, w_down: torch.Tensor) -> MoEFP8Weights:
+    """Per-output-channel e4m3 quantisation of the layer's weights (done once, on the GPU)."""
+    from grouped_gemm_opt.ops import quantize_fp8
+    gq, gs = quantize_fp8(w_gate_up)
+    dq, ds = quantize_fp8(w_down)
+    return MoEFP8Weights(gq, gs, dq, ds)
+
+
+def fused_moe_fp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: MoEFP8Weights,
+                  top_k: int, sort_by_m: bool = True) -> torch.Tensor:
+    """Single-GPU MoE layer with FP8 (e4m3) grouped GEMMs: route -> dispatch -> per-row
+    quantisation of the gathered rows -> gate/up GEMM with a scaled SwiGLU epilogue (bf16 h) ->
+    per-row quantisation of h -> down GEMM with a scaled epilogue -> combine. Routing, dispatch
+    and combine are the bf16 layer's; the result is bf16."""
+    from grouped_gemm_opt._native import _C
+    E = router_logits.size(1)
+    assert weights.w_gate_up_q.size(0) == E, "all experts must be local"
+    ids, w, tpe, scratch = _C.moe_route(router_logits, top_k)
+    xs, _, slot_pos = _C.moe_permute(hidden.contiguous(), ids, scratch, E)
+    xq, xsc = _C.quantize_fp8_rows(xs)
+    h = _C.grouped_gemm_swiglu_fp8(xq, xsc, weights.w_gate_up_q, weights.w_gate_up_scale, tpe, E,
+                                   sort_by_m)
+    hq, hsc = _C.quantize_fp8_rows(h)
+    y = _C.grouped_gemm_fp8(hq, hsc, weights.w_down_q, weights.w_down_scale, tpe, 4, sort_by_m)
+    return _C.moe_combine(y, w, slot_pos)

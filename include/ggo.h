@@ -139,6 +139,17 @@ int ggo_grouped_gemm_fp8(const void* input_dev, const float* input_scale_dev,
                          int64_t total_tokens, int64_t N, int64_t K, int tile_config,
                          int sort_by_m, void* workspace_dev, cudaStream_t stream);
 
+/* FP8 gate/up grouped GEMM with the SwiGLU epilogue (no reference counterpart):
+ *   h[r, f] = silu(g * s_x[r] * s_w[e, f]) * (u * s_x[r] * s_w[e, F + f])  (bf16 out)
+ * with g / u the e4m3 dot products of x row r with weight rows f / F + f. x [T, K] and
+ * w_gate_up [E, 2F, K] e4m3; x_scale [T], w_scale [E, 2F] fp32. Segment semantics as
+ * ggo_grouped_gemm_segments. K a multiple of 16, F of 8. */
+int ggo_grouped_gemm_swiglu_fp8(const void* x_dev, const float* x_scale_dev,
+                                const void* w_gate_up_dev, const float* w_scale_dev, void* h_dev,
+                                const int64_t* tokens_per_segment_dev, int num_segments,
+                                int num_experts, int64_t total_tokens, int64_t F, int64_t K,
+                                int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
 /* Row-wise e4m3 quantisation of a bf16/fp16 matrix [rows, cols]: scale_dev[r] =
  * max|x[r,:]| / 448 (1 for an all-zero row), q_dev[r,c] = e4m3(x[r,c] / scale[r]) rounded to
  * nearest with saturation. Weights [E, N, K] quantise per output channel as rows = E*N.

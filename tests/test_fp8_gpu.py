@@ -47,3 +47,42 @@ def test_fp8_grouped_gemm(tc, counts, k, n):
     assert_parity(out, oracle.sequential_gemm(xd, wd, tpe), f"fp8 tc={tc}")
     rel, cos = parity(out, oracle.sequential_gemm(x, w, tpe))
     assert rel < 0.1 and cos > 0.998, (rel, cos)  # e4m3 quantisation error vs the bf16 GEMM
+
+
+def test_swiglu_fp8():
+    from grouped_gemm_opt import _C, quantize_fp8
+    x, w, tpe = gemm_inputs([2000, 0, 3000, 77], 256, 1024, seed=2)  # F = 512
+    xq, xs = quantize_fp8(x.to(DEV))
+    wq, ws = quantize_fp8(w.to(DEV))
+    h = _C.grouped_gemm_swiglu_fp8(xq, xs, wq, ws, tpe.to(DEV), 4, True)
+    xd = xq.cpu().float() * xs.cpu().unsqueeze(1)
+    wd = wq.cpu().float() * ws.cpu().unsqueeze(-1)
+    assert_parity(h, oracle.swiglu_gemm(xd, wd, tpe, 4), "swiglu fp8")
+
+
+def test_fused_moe_fp8():
+    """FP8 layer vs the same quantisation steps on the CPU (dequantised operands, fp32 math)."""
+    import numpy as np
+    from grouped_gemm_opt import fused_moe_fp8, quantize_moe_weights
+    g = torch.Generator().manual_seed(9)
+    T, H, F, E, k = 512, 512, 1024, 8, 2
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g)
+    wgu = (torch.randn(E, 2 * F, H, generator=g) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(E, H, F, generator=g) * 0.02).to(torch.bfloat16)
+    qw = quantize_moe_weights(wgu.to(DEV), wd.to(DEV))
+    out = fused_moe_fp8(x.to(DEV), logits.to(DEV), qw, k)
+    # CPU restatement of the FP8 pipeline
+    ids, w, tpe = oracle.route(logits.numpy(), k)
+    st, pos = oracle.permute_indices(ids, E)
+    xs = x[torch.from_numpy(st).long()]
+    xq, xsc = _ref_quant(xs)
+    gud = qw.w_gate_up_q.cpu().float() * qw.w_gate_up_scale.cpu().unsqueeze(-1)
+    h = oracle.swiglu_gemm(xq.float() * xsc.unsqueeze(1), gud, torch.from_numpy(tpe), E)
+    hq, hsc = _ref_quant(h.to(torch.bfloat16))
+    dd = qw.w_down_q.cpu().float() * qw.w_down_scale.cpu().unsqueeze(-1)
+    y = oracle.segments_gemm(hq.float() * hsc.unsqueeze(1), dd, torch.from_numpy(tpe), E)
+    ref = oracle.combine(y.to(torch.bfloat16), w, pos)
+    assert_parity(out, ref, "fused moe fp8")
+    rel, cos = parity(out, oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.bfloat16))
+    assert cos > 0.995, cos  # vs the bf16 layer: e4m3 quantisation error only
