@@ -398,6 +398,26 @@ def config_sweep(steps=60, warmup=5):
     res["cfg2_fp8"] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
     del x, dy, w, xq, wq
     torch.cuda.empty_cache()
+    # Mixtral layer with FP8 (e4m3) grouped GEMMs on one GPU (the bf16 one is `moe_layer`)
+    from grouped_gemm_opt import fused_moe_fp8, quantize_moe_weights
+    T2, H2, F2, E2, k2 = 16384, 4096, 14336, 8, 2
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(T2, H2, device="cuda", generator=g).to(torch.bfloat16)
+    logits = torch.randn(T2, E2, device="cuda", generator=g)
+    qw = quantize_moe_weights(
+        (torch.randn(E2, 2 * F2, H2, device="cuda", generator=g) * 0.02).to(torch.bfloat16),
+        (torch.randn(E2, H2, F2, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+    torch.cuda.empty_cache()
+    fn = lambda: fused_moe_fp8(x, logits, qw, k2)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    st = max(3, steps // 4)
+    total, _ = _timed(fn, st, 1)
+    ms = total / st
+    res["mixtral_layer_fp8"] = {"ms": ms, "tokens_per_s": T2 / ms * 1e3,
+                                "tflops": 6.0 * T2 * k2 * H2 * F2 / ms / 1e9}
+    del x, qw
+    torch.cuda.empty_cache()
     # DeepSeek-V3-shaped layer on one GPU (all 256 experts local): decode and prefill token counts
     for name, T in (("dsv3_layer_T256", 256), ("dsv3_layer_T32768", 32768)):
         H, F, ex, k = 7168, 2048, 256, 8
