@@ -215,6 +215,40 @@ def run_reference(args):
     }), flush=True)
 
 
+def dsv3_ep_bench(world, rank, steps, warmup):
+    """BASELINE configs[4] at N>1: DeepSeek-V3-shaped layer (H=7168, F=2048, E=256, top-8),
+    expert-parallel over the ranks on the fused peer-memory path, at T=32768 and the decode-like
+    T=256 (tokens in total, split over ranks). Whole-job tokens/s, max-over-ranks device time."""
+    import torch
+    import torch.distributed as dist
+    from grouped_gemm_opt import EPBuffers, fused_moe
+    H, F, Ex, k = 7168, 2048, 256, 8
+    el = Ex // world
+    g = torch.Generator(device="cuda").manual_seed(2000 + rank)
+    wgu = (torch.randn(el, 2 * F, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(el, H, F, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    out = {}
+    for T in (32768, 256):
+        tl = T // world
+        x = torch.randn(tl, H, device="cuda", generator=g).to(torch.bfloat16)
+        logits = torch.randn(tl, Ex, device="cuda", generator=g)
+        bufs = EPBuffers(dist.group.WORLD, tl, H, k, Ex, torch.bfloat16)
+        fn = lambda: fused_moe(x, logits, wgu, wd, k, ep_group=dist.group.WORLD,  # noqa: E731
+                               ep_buffers=bufs)
+        for _ in range(warmup):
+            fn()
+        total_ms, _ = _timed(fn, steps, world)
+        bufs.close()
+        ms = total_ms / steps
+        out[f"T{T}"] = {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
+                        "tflops": 6.0 * T * k * H * F / (ms / 1e3) / 1e12,
+                        "weight_gbs_per_gpu": 3.0 * el * F * H * 2 / (ms / 1e3) / 1e9}
+        del x, logits
+        torch.cuda.empty_cache()
+    return {"workload": "DSv3 MoE layer H7168 F2048 E256 top8, fused EP path",
+            "parallelism": f"ep{world}", **out}
+
+
 def moe_layer_bench(world, rank, steps, warmup):
     """Expert-parallel Mixtral layer: T=16384 tokens in total (split over ranks), H=4096,
     F=14336, E=8, top-2. Returns tokens/s of the whole job (max-over-ranks device time). With
@@ -557,6 +591,8 @@ def main():
         del out["y"]
         torch.cuda.empty_cache()
         moe = moe_layer_bench(world, rank, max(3, min(50, args.steps // 20)), 3)
+        if world > 1:
+            moe["dsv3"] = dsv3_ep_bench(world, rank, max(3, min(20, args.steps // 50)), 3)
 
     sweep = None
     if world == 1 and not args.no_sweep:
