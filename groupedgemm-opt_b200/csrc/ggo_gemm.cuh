@@ -397,6 +397,10 @@ __device__ __forceinline__ void load_out32(uint32_t t_row, int c, uint32_t (&o)[
 //    the 128-B swizzle: 16-B chunk j of row r at chunk j ^ (r % 8), conflict-free) and written
 //    with one TMA store; the box at x0 = n0 + c64, y0 = x_row0. Columns past n_out are clipped by
 //    the tensor map.
+//  * row_copy (scatter epilogue, rows going to scattered destinations, often another GPU): the
+//    box is staged the same way, then copied out row by row -- eight lanes write one row's 128
+//    contiguous bytes -- so each store instruction sends whole rows instead of 16-byte pieces of
+//    32 different rows.
 //  * otherwise each thread stores its own row with 16-byte stores, masked by row_ok and n_out.
 template <int BN, int EPI, bool BF16, typename OutT>
 __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_out, bool row_ok,
@@ -404,10 +408,11 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
                                                 const CUtensorMap* tmC, uint8_t* stage,
                                                 int x_row0, float rs = 1.f,
                                                 const float* cs_row = nullptr,
-                                                int cs_up_off = 0) {
+                                                int cs_up_off = 0, bool row_copy = false) {
   constexpr int OUTW = epi_glu(EPI) ? BN / 2 : BN;
   const int lane = threadIdx.x & 31;
   const uint32_t st_row = smem_u32(stage) + lane * 128;
+  const bool staged = warp_tma || row_copy;
 #pragma unroll 1
   for (int c64 = 0; c64 < OUTW; c64 += 64) {
     if (warp_tma && c64 > 0) {  // the previous box's store has read the staging buffer
@@ -421,7 +426,7 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
       uint32_t o[16];
       load_out32<BN, EPI, BF16>(t_row, c, o, rs, cs_row ? cs_row + n0 + c : nullptr,
                                 n_out - (n0 + c), cs_up_off);
-      if (warp_tma) {
+      if (staged) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const uint32_t chunk = static_cast<uint32_t>((4 * s + q) ^ (lane & 7));
@@ -444,6 +449,24 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
         tma_store_2d(tmC, stage, n0 + c64, x_row0);
         bulk_commit();
       }
+    } else if (row_copy) {
+      __syncwarp();
+      const int box_cols = OUTW - c64 < 64 ? OUTW - c64 : 64;
+      const int chunk = lane & 7;
+      const uint32_t base = smem_u32(stage);
+#pragma unroll 1
+      for (int it = 0; it < 8; ++it) {
+        const int row = it * 4 + (lane >> 3);
+        const unsigned long long rp =
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(out_row), row);
+        const int rok = __shfl_sync(0xffffffffu, row_ok ? 1 : 0, row);
+        const int col = n0 + c64 + chunk * 8;
+        if (rok && chunk * 8 < box_cols && col < n_out) {
+          const uint4 v = ld_shared_v4(base + row * 128 + ((chunk ^ (row & 7)) * 16));
+          *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(rp) + col) = v;
+        }
+      }
+      __syncwarp();  // the next box reuses the staging buffer
     }
   }
 }
@@ -653,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           kScaled ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_b : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
                                      staging + ew * 4096, info.row0 + ew * 32, rs, cs_row,
-                                     p.n_b / 2);
+                                     p.n_b / 2, p.origin != nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[acc]);

@@ -253,7 +253,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           kScaled ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_b : nullptr;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
                                      staging + ew * 4096, info.row0 + wrow0, rs, cs_row,
-                                     p.n_b / 2);
+                                     p.n_b / 2, p.origin != nullptr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));

@@ -144,3 +144,35 @@ def test_fused_moe_fp16():
     assert out.dtype == torch.float16
     ref = oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.float16)
     assert_parity(out, ref, "fused_moe fp16")
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_scatter_epilogue_single_gpu(C, swiglu):
+    """The expert-parallel scatter epilogue with this GPU as the only 'peer': row r of the GEMM
+    must land at row origin[r] (& 0x0fffffff) of the target buffer; rows are a random
+    permutation, segments [expert-major], capacity larger than the counted rows."""
+    counts = [300, 7, 0, 513, 129]
+    n_out, k = 256, 512
+    x, w, tpe = gemm_inputs(counts, k, 2 * n_out if swiglu else n_out, seed=31)
+    rows = x.size(0)
+    cap = rows + 100
+    xc = torch.zeros(cap, k, dtype=torch.bfloat16)
+    xc[:rows] = x
+    perm = torch.randperm(rows, generator=torch.Generator().manual_seed(3)).to(torch.int32)
+    origin = torch.zeros(cap, dtype=torch.int32)
+    origin[:rows] = perm  # source rank 0 in the top bits
+    target = torch.zeros(rows, n_out, dtype=torch.bfloat16, device=DEV)
+    if swiglu:
+        ref = oracle.swiglu_gemm(x, w, tpe, len(counts))
+        h = C.ep_grouped_gemm(xc.to(DEV), w.to(DEV), tpe.to(DEV), len(counts), True, None, [],
+                              True)
+        out = h[:rows]
+    else:
+        ref = oracle.segments_gemm(x, w, tpe, len(counts))
+        C.ep_grouped_gemm(xc.to(DEV), w.to(DEV), tpe.to(DEV), len(counts), False,
+                          origin.to(DEV), [target.data_ptr()], True)
+        torch.cuda.synchronize()
+        out = torch.empty_like(target)
+        out[:] = 0
+        out = target[perm.long().to(DEV)]
+    assert_parity(out, ref, f"scatter swiglu={swiglu}")
