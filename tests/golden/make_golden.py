@@ -6,13 +6,19 @@ Run in a container where the reference checkout is available (it is not on the G
 
 It imports the reference's ``benchmarks/benchmark.py`` and calls its ground-truth
 ``sequential_gemm`` (benchmark.py:91-107) and its routing generators ``uniform_distribution`` /
-``skewed_distribution`` (benchmark.py:50-69) on CPU tensors. Inputs are regenerated from seeds by
+``skewed_distribution`` (benchmark.py:50-69) on CPU tensors. It also runs the reference's own
+Triton kernels ``triton_grouped_gemm`` (grouped_gemm_opt/triton_grouped_gemm.py:139-197) and
+``triton_fused_moe`` (grouped_gemm_opt/triton_fused_moe.py:104-150) on the CPU under Triton's
+interpreter (TRITON_INTERPRET=1, fp32 inputs; the interpreter does not support bf16 here) and
+stores checksums of their outputs. Inputs are regenerated from seeds by
 ``tests/golden/inputs.py`` (stored here as SHA-256 digests so drift is detected); outputs are
 stored as raw bf16 bits (small cases) or as checksums plus a strided sample (cfg1).
 """
 from __future__ import annotations
 
 import hashlib
+import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -56,6 +62,27 @@ def main(ref_root: str) -> None:
         out[f"edge_{name}_x_sha"] = np.array(_digest(x))
         out[f"edge_{name}_w_sha"] = np.array(_digest(w))
         out[f"edge_{name}_y_bits"] = _bits(y)
+
+    # the reference's Triton kernels under the interpreter (fp32), on the edge cases
+    os.environ["TRITON_INTERPRET"] = "1"
+
+    def load(name, rel):
+        spec = importlib.util.spec_from_file_location(name, str(Path(ref_root) / rel))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+
+    tgg = load("ref_triton_grouped_gemm", "grouped_gemm_opt/triton_grouped_gemm.py")
+    tfm = load("ref_triton_fused_moe", "grouped_gemm_opt/triton_fused_moe.py")
+    for name, counts in EDGE_CASES.items():
+        x, w, tpe = edge_inputs(counts)
+        xf, wf = x.float(), w.float()
+        y = tgg.triton_grouped_gemm(xf, wf, tpe, BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
+        yf = tfm.triton_fused_moe(xf, wf, tpe, BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
+        for tag, t in (("tgg", y), ("tfm", yf)):
+            out[f"{tag}_{name}_row_sum"] = t.double().sum(1).numpy()
+            out[f"{tag}_{name}_col_sum"] = t.double().sum(0).numpy()
+            out[f"{tag}_{name}_sample"] = t.reshape(-1)[::37].numpy()
 
     # routing generators
     for T, E in [(4096, 8), (8192, 64), (1000, 7), (16384, 256)]:

@@ -75,3 +75,42 @@ def test_moe_validation(lib):
     assert f(p, 16, 8, 9, p, p, p, p, None) == 1     # top_k > E
     assert f(p, 16, 2048, 2, p, p, p, p, None) == 1  # E > 1024
     assert f(None, 16, 8, 2, p, p, p, p, None) == 1
+
+
+C_PROGRAM = r"""
+#include <stdio.h>
+#include <string.h>
+#include "ggo.h"
+int main(void) {
+  /* metadata and host-side validation only: no GPU is needed for these paths */
+  if (ggo_version() != 100) return 1;
+  if (ggo_workspace_size() != GGO_WORKSPACE_BYTES) return 2;
+  if (strlen(ggo_status_string(GGO_ERR_ALIGNMENT)) == 0) return 3;
+  char dummy[64];
+  int st = ggo_grouped_gemm(NULL, dummy, dummy, (const int64_t*)dummy, 8, 256, 1024, 512,
+                            GGO_DTYPE_BF16, GGO_TILE_AUTO, 1, dummy, (cudaStream_t)0);
+  if (st != GGO_ERR_INVALID_ARG) return 4;
+  st = ggo_grouped_gemm_noalloc(dummy, dummy, dummy, (const int64_t*)dummy,
+                                GGO_NOALLOC_MAX_EXPERTS + 1, 16, 64, 64, GGO_DTYPE_BF16,
+                                GGO_TILE_AUTO, 1, (cudaStream_t)0);
+  if (st != GGO_ERR_TOO_MANY_SEGMENTS) return 5;
+  printf("ok\n");
+  return 0;
+}
+"""
+
+
+def test_header_is_plain_c(tmp_path):
+    """include/ggo.h compiles as C99 and a C program links and runs against libggo_b200.so."""
+    import subprocess
+    src = tmp_path / "abi.c"
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / "abi"
+    inc = os.path.dirname(HEADER)
+    libdir = os.path.dirname(str(lib_path()))
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", inc, "-I",
+                        "/usr/local/cuda/include", str(src), "-o", str(exe), f"-L{libdir}",
+                        "-lggo_b200", f"-Wl,-rpath,{libdir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stderr)

@@ -106,3 +106,30 @@ def test_route_tie_break_lower_index():
     ids, w, _ = oracle.route(logits, 3)
     assert ids.tolist() == [[0, 1, 2], [0, 1, 2]]
     assert np.allclose(w, 1 / 3)
+
+
+@pytest.mark.parametrize("name", list(EDGE_CASES))
+def test_oracle_matches_reference_triton_grouped_gemm(name):
+    """The reference's own triton_grouped_gemm (run in Triton's CPU interpreter, fp32) agrees with
+    the oracle: a second, independent pin of the grouped-GEMM semantics."""
+    x, w, tpe = edge_inputs(EDGE_CASES[name])
+    y = oracle.sequential_gemm(x, w, tpe).double()
+    np.testing.assert_allclose(y.sum(1).numpy(), GOLDEN[f"tgg_{name}_row_sum"], atol=1e-3)
+    np.testing.assert_allclose(y.sum(0).numpy(), GOLDEN[f"tgg_{name}_col_sum"], atol=1e-3)
+    np.testing.assert_allclose(y.reshape(-1)[::37].numpy(), GOLDEN[f"tgg_{name}_sample"],
+                               rtol=1e-5, atol=1e-5)
+
+
+def test_reference_triton_fused_moe_bug_is_not_reproduced():
+    """The reference's triton_fused_moe handles at most 4 experts per 128-row tile
+    (triton_fused_moe.py:54-73, 131); on a tile spanning more it computes wrong rows. The fixture
+    holds its output: it differs from the oracle there (and only there), while this library's
+    triton_fused_moe follows the oracle (GPU test test_triton_aliases)."""
+    for name in EDGE_CASES:
+        x, w, tpe = edge_inputs(EDGE_CASES[name])
+        y = oracle.sequential_gemm(x, w, tpe).double()
+        dev = np.abs(y.reshape(-1)[::37].numpy() - GOLDEN[f"tfm_{name}_sample"]).max()
+        if name == "span_gt4":
+            assert dev > 0.1, dev
+        else:
+            assert dev < 1e-4, (name, dev)
