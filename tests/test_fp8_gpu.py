@@ -86,3 +86,23 @@ def test_fused_moe_fp8():
     assert_parity(out, ref, "fused moe fp8")
     rel, cos = parity(out, oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.bfloat16))
     assert cos > 0.995, cos  # vs the bf16 layer: e4m3 quantisation error only
+
+
+def test_fp8_cfg2_full_size_sampled():
+    from grouped_gemm_opt import grouped_gemm_opt_fp8, quantize_fp8
+    T, E, K, N = 4096, 8, 4096, 14336
+    tpe = torch.full((E,), 512)
+    g = torch.Generator(device=DEV).manual_seed(6)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    xq, xs = quantize_fp8(x)
+    wq, ws = quantize_fp8(w)
+    out = grouped_gemm_opt_fp8(xq, xs, wq, ws, tpe.to(DEV))
+    rows = torch.arange(3, T, 97)
+    ref = []
+    for r in rows.tolist():
+        e = r // 512
+        a = xq[r].float().cpu() * xs[r].cpu()
+        b = wq[e].float().cpu() * ws[e].cpu().unsqueeze(1)
+        ref.append(b @ a)
+    assert_parity(out[rows.to(DEV)], torch.stack(ref), "fp8 cfg2")

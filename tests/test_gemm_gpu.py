@@ -338,3 +338,27 @@ def test_dgrad_wgrad_fp16(tc):
     for e, m in enumerate(counts):
         if m:
             assert_parity(dw[e], ref[e], f"wgrad fp16 {e}")
+
+
+def test_backward_cfg2_full_size_sampled():
+    """dgrad and wgrad at the cfg2 shapes (E=8, T=4096, K=4096, N=14336), checked on samples:
+    dx rows (each row is independent) and dW columns of one expert."""
+    from grouped_gemm_opt import _C
+    T, E, K, N = 4096, 8, 4096, 14336
+    tpe = torch.tensor([512, 480, 520, 500, 510, 490, 530, 554])
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    dy = torch.randn(T, N, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    dx = _C.grouped_gemm_dgrad(dy, w, tpe.to(DEV), 4, True)
+    rows = _sample_rows(tpe, 4)
+    ex = torch.searchsorted(torch.cumsum(tpe, 0), rows, right=True)
+    ref = torch.stack([dy[int(r)].float().cpu() @ w[int(e)].float().cpu()
+                       for r, e in zip(rows, ex)])
+    assert_parity(dx[rows.to(DEV)], ref, "dgrad cfg2")
+    dw = _C.grouped_gemm_wgrad(x, dy, tpe.to(DEV), True)
+    e = 7
+    off = int(tpe[:e].sum())
+    cols = torch.randint(0, K, (16,), generator=torch.Generator().manual_seed(1))
+    ref = dy[off:off + 554].float().cpu().T @ x[off:off + 554][:, cols.to(DEV)].float().cpu()
+    assert_parity(dw[e][:, cols.to(DEV)], ref, "wgrad cfg2 expert 7")
