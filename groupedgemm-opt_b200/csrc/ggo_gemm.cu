@@ -74,6 +74,21 @@ int make_map_fp8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int 
   return make_map_dt(m, base, rows, k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, box_rows, 128);
 }
 
+// Block-scale map (MX path): the UE8M0 scales as [atoms * 2, 256] bytes, no swizzle, boxes of
+// one 512-B atom (2 x 256). Atoms past the end read as zeros.
+int make_sf_map(CUtensorMap* m, const void* base, int64_t atoms) {
+  EncodeTiledFn enc;
+  if (int st = get_encode(&enc)) return st;
+  const cuuint64_t dims[2] = {256, static_cast<cuuint64_t>(atoms > 0 ? 2 * atoms : 2)};
+  const cuuint64_t strides[1] = {256};
+  const cuuint32_t box[2] = {256, 2};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? GGO_OK : cuda_fail(100000 + static_cast<int>(r));
+}
+
 // Output map for the TMA-store epilogue: [rows, n_out] row-major, boxes of 32 rows x 64 columns
 // (128 B, 128-B swizzle, matching the staging layout). Only for a plain (non-scattered) output.
 int make_out_map(CUtensorMap* m, GemmParams* p, bool bf16) {
@@ -149,10 +164,25 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   return check_launch();
 }
 
-template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
+// Block scales of an MX launch: base pointers and their sizes in 512-B atoms.
+struct MxScales {
+  const void* a = nullptr;
+  int64_t a_atoms = 0;
+  const void* b = nullptr;
+  int64_t b_atoms = 0;
+};
+
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false, bool MX = false>
 int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
-                cudaStream_t stream) {
-  CUtensorMap ma, mb, mc;
+                cudaStream_t stream, const MxScales* mx = nullptr) {
+  CUtensorMap ma, mb, mc, msa, msb;
+  memset(&msa, 0, sizeof(msa));
+  memset(&msb, 0, sizeof(msb));
+  if (MX) {
+    if (!mx) return GGO_ERR_INVALID_ARG;
+    if (int st = make_sf_map(&msa, mx->a, mx->a_atoms)) return st;
+    if (int st = make_sf_map(&msb, mx->b, mx->b_atoms)) return st;
+  }
   GemmParams q = p;
   if (FP8) {
     if (int st = make_map_fp8(&ma, a, q.rows, q.k, 128)) return st;
@@ -162,8 +192,8 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
     if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, BN / 2)) return st;
   }
   if (int st = make_out_map(&mc, &q, BF16)) return st;
-  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16, BMN, FP8>;
-  constexpr int smem = PairLayout<BN>::kTotal;
+  auto kern = grouped_gemm_pair_kernel<BN, EPI, BF16, BMN, FP8, MX>;
+  constexpr int smem = PairLayout<BN, MX>::kTotal;
   int clusters = 0;
   if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
   constexpr int out_bn = epi_glu(EPI) ? BN / 2 : BN;
@@ -171,7 +201,7 @@ int launch_pair(const void* a, const void* b, int64_t b_rows, const GemmParams& 
   const int64_t ub = ((p.rows + 255) / 256 + p.num_segments) * n_tiles;  // pair-tile upper bound
   const int64_t pairs = ub < clusters ? ub : clusters;
   if (pairs <= 0) return GGO_OK;
-  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, mc, q);
+  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(ma, mb, mc, msa, msb, q);
   return check_launch();
 }
 
@@ -266,7 +296,23 @@ struct GemmExtras {
   int fp8 = 0;
   const float* row_scale = nullptr;
   const float* col_scale = nullptr;
+  // MX path (with fp8): e4m3 operands with UE8M0 block scales (one per 32 K elements) in the
+  // 128x4 blocked layout, applied by the tensor cores; out = the block-scaled product in bf16
+  int mx = 0;
+  const void* a_sf = nullptr;
+  const void* b_sf = nullptr;
 };
+
+// MX tiles: CTA pairs of 256 x 192 (192 columns leave TMEM room for the scales next to two
+// accumulators). SwiGLU weights for the MX path are blocked by kMxGluBlock output columns:
+// [E, 2 * F_pad, K], F_pad = F rounded up to kMxGluBlock, block j = gate rows j*96.. then up rows.
+constexpr int kMxPairBN = 192;
+constexpr int kMxGluBlock = kMxPairBN / 2;
+int64_t mx_glu_rows(int64_t f) { return 2 * ((f + kMxGluBlock - 1) / kMxGluBlock) * kMxGluBlock; }
+// 512-B scale atoms of `rows` rows in `segments` segments (each padded to 128 rows), K columns
+int64_t mx_scale_atoms(int64_t rows, int64_t segments, int64_t k) {
+  return ((rows + 127) / 128 + segments) * (k / 128);
+}
 
 int gemm_common(const void* input, const void* weights, void* output, const int64_t* counts,
                 int num_segments, int num_experts, int64_t rows, int64_t n, int64_t k, int dtype,
@@ -286,17 +332,22 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   if (tile_config < 0 || tile_config > GGO_TILE_CUBLAS_SEQ) return GGO_ERR_INVALID_ARG;
   if (num_segments > kMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
   const bool fp8 = ex && ex->fp8;
+  const bool mx = fp8 && ex->mx;
   if (fp8) {
-    if (!ex->row_scale || !ex->col_scale || bmn || scatter) return GGO_ERR_INVALID_ARG;
+    if (bmn || scatter) return GGO_ERR_INVALID_ARG;
+    if (mx ? (!ex->a_sf || !ex->b_sf) : (!ex->row_scale || !ex->col_scale))
+      return GGO_ERR_INVALID_ARG;
     dtype = GGO_DTYPE_BF16;  // e4m3 in, bf16 out
-    if (k % 16) return GGO_ERR_ALIGNMENT;  // rows of K bytes must be 16-byte multiples
+    if (k % (mx ? 128 : 16)) return GGO_ERR_ALIGNMENT;  // rows of K bytes; MX: whole scale atoms
+    if (mx && (!aligned16(ex->a_sf) || !aligned16(ex->b_sf))) return GGO_ERR_ALIGNMENT;
   }
   if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
   if ((k % 8) || (n % 8)) return GGO_ERR_ALIGNMENT;
   if (!aligned16(input) || !aligned16(weights) || (output && !aligned16(output)) ||
       (reinterpret_cast<uintptr_t>(workspace) & 3u))
     return GGO_ERR_ALIGNMENT;
-  const int64_t b_rows = static_cast<int64_t>(num_experts) * (swiglu ? 2 * n : n);
+  const int64_t n_b = swiglu ? (mx ? mx_glu_rows(n) : 2 * n) : n;
+  const int64_t b_rows = static_cast<int64_t>(num_experts) * n_b;
   if (rows > INT32_MAX || b_rows > INT32_MAX || k > INT32_MAX) return GGO_ERR_SHAPE;
   if (bmn && static_cast<int64_t>(num_experts) * k > INT32_MAX) return GGO_ERR_SHAPE;
   if (rows == 0) return GGO_OK;
@@ -309,7 +360,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.num_experts = num_experts;
   p.rows = static_cast<int>(rows);
   p.n_out = static_cast<int>(n);
-  p.n_b = static_cast<int>(swiglu ? 2 * n : n);
+  p.n_b = static_cast<int>(n_b);
   p.k = static_cast<int>(k);
   p.sort_by_m = sort_by_m ? 1 : 0;
   p.group_m = raster_group_m(k, 128);  // re-derived below for 256-row pair tiles
@@ -321,6 +372,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.split_mode = 0;
   p.split_tail_ntiles = 1;
   p.split_min_tiles = 0;
+  p.glu_blocked = 0;
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.row_scale = fp8 ? ex->row_scale : nullptr;
   p.col_scale = fp8 ? ex->col_scale : nullptr;
@@ -330,6 +382,19 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.ws = static_cast<GgoWorkspace*>(workspace);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
   int bn = choose_bn(tile_config, rows, swiglu ? 2 * n : n, num_segments, g_sm_count[dev]);
+  if (mx) {  // CTA pairs only (no short-tail pass: its scales would need a second layout)
+    MxScales sc;
+    sc.a = ex->a_sf;
+    sc.a_atoms = mx_scale_atoms(rows, num_segments, k);
+    sc.b = ex->b_sf;
+    sc.b_atoms = static_cast<int64_t>(num_experts) * ((n_b + 127) / 128) * (k / 128);
+    p.group_m = raster_group_m(k / 2, 256);
+    p.glu_blocked = swiglu ? 1 : 0;
+    return swiglu ? launch_pair<kMxPairBN, kEpiSwiGLU, true, false, true, true>(
+                        input, weights, b_rows, p, dev, stream, &sc)
+                  : launch_pair<kMxPairBN, kEpiStore, true, false, true, true>(
+                        input, weights, b_rows, p, dev, stream, &sc);
+  }
   if (fp8) {  // CTA-pair pass (+ short-tail pass) or single-CTA 128x256, scaled epilogue
     if (bn == 512) {
       const bool split = env_int("GGO_SPLIT_TAILS", 1) > 0;
@@ -583,6 +648,43 @@ int ggo_grouped_gemm_swiglu_fp8(const void* x_dev, const float* x_scale_dev,
   ex.fp8 = 1;
   ex.row_scale = x_scale_dev;
   ex.col_scale = w_scale_dev;
+  return ggo::gemm_common(x_dev, w_gate_up_dev, h_dev, tokens_per_segment_dev, num_segments,
+                          num_experts, total_tokens, F, K, GGO_DTYPE_BF16, GGO_TILE_AUTO,
+                          sort_by_m, workspace_dev, stream, true, &ex);
+}
+
+size_t ggo_mxfp8_scale_bytes(int64_t rows, int num_segments, int64_t k) {
+  if (rows < 0 || num_segments < 0 || k <= 0 || k % 128) return 0;
+  return static_cast<size_t>(ggo::mx_scale_atoms(rows, num_segments, k)) * 512;
+}
+
+int64_t ggo_mxfp8_glu_rows(int64_t F) { return F > 0 ? ggo::mx_glu_rows(F) : 0; }
+
+int ggo_grouped_gemm_mxfp8(const void* input_dev, const void* input_scale_dev,
+                           const void* weights_dev, const void* weight_scale_dev, void* output_dev,
+                           const int64_t* tokens_per_segment_dev, int num_segments,
+                           int num_experts, int64_t total_tokens, int64_t N, int64_t K,
+                           int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  ggo::GemmExtras ex;
+  ex.fp8 = 1;
+  ex.mx = 1;
+  ex.a_sf = input_scale_dev;
+  ex.b_sf = weight_scale_dev;
+  return ggo::gemm_common(input_dev, weights_dev, output_dev, tokens_per_segment_dev, num_segments,
+                          num_experts, total_tokens, N, K, GGO_DTYPE_BF16, GGO_TILE_AUTO,
+                          sort_by_m, workspace_dev, stream, false, &ex);
+}
+
+int ggo_grouped_gemm_swiglu_mxfp8(const void* x_dev, const void* x_scale_dev,
+                                  const void* w_gate_up_dev, const void* w_scale_dev, void* h_dev,
+                                  const int64_t* tokens_per_segment_dev, int num_segments,
+                                  int num_experts, int64_t total_tokens, int64_t F, int64_t K,
+                                  int sort_by_m, void* workspace_dev, cudaStream_t stream) {
+  ggo::GemmExtras ex;
+  ex.fp8 = 1;
+  ex.mx = 1;
+  ex.a_sf = x_scale_dev;
+  ex.b_sf = w_scale_dev;
   return ggo::gemm_common(x_dev, w_gate_up_dev, h_dev, tokens_per_segment_dev, num_segments,
                           num_experts, total_tokens, F, K, GGO_DTYPE_BF16, GGO_TILE_AUTO,
                           sort_by_m, workspace_dev, stream, true, &ex);

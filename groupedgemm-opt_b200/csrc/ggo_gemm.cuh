@@ -95,6 +95,10 @@ struct GemmParams {
   int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
   int split_tail_ntiles;  // column tiles of the tail pass (its output width / its tile width)
   int split_min_tiles;    // split only when the tail pass gets at least this many tiles
+  // SwiGLU weight layout: 0 = all gate rows then all up rows; 1 = blocked, output columns
+  // [n0, n0 + w) read weight rows [2 n0, 2 n0 + 2w): w gate rows then the w matching up rows,
+  // w = the tile's output width (the layout the MX path's weight preparation writes)
+  int glu_blocked;
   GgoWorkspace* ws;
 };
 
@@ -309,6 +313,9 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     // MN-major weights [E, Kred, n_out]: rows are the reduction index; the column is n0
     info.brow0 = expert * p.k;
     info.brow1 = info.brow0;
+  } else if (epi_glu(EPI) && p.glu_blocked) {
+    info.brow0 = expert * p.n_b + 2 * info.n0;  // gate rows, then the up rows of the same block
+    info.brow1 = info.brow0 + B_HALF;
   } else if (epi_glu(EPI)) {
     info.brow0 = expert * p.n_b + info.n0;                 // gate rows
     info.brow1 = expert * p.n_b + (p.n_b >> 1) + info.n0;  // matching up rows

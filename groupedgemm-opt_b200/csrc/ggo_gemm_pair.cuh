@@ -20,13 +20,18 @@
 
 namespace ggo {
 
-template <int BN>
+template <int BN, bool MX = false>
 struct PairLayout {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 A rows
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of the BN-row B tile
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  // MX: this CTA's A scales (one 512-B atom: 128 rows x 4 K groups of 32) and the scales of the
+  // 256 weight rows around the tile (two atoms), behind the B half
+  static constexpr int kSfBytes = MX ? 3 * 512 : 0;
+  static constexpr int kTxBytes = kABytes + kBBytes + kSfBytes;  // one CTA's loads per stage
+  static constexpr int kStageBytes = (kTxBytes + 1023) / 1024 * 1024;  // 1024-B aligned stages
   static constexpr int kStagingBytes = 4 * 4096;  // TMA-store staging, 4 KB per epilogue warp
-  static constexpr int kTableBytes = 4 * kMaxSegments * 4 + 16;
+  // segment tables: counts, row offsets, order, tile offsets (+1), and for MX the scale blocks
+  static constexpr int kTableBytes = MX ? 5 * kMaxSegments * 4 + 32 : 4 * kMaxSegments * 4 + 16;
   static constexpr int kMiscBytes = 1024;
   // as many stages (<= 8) as fit in the 227 KB a CTA may use, after everything else
   static constexpr int kRingBudget = 227 * 1024 - 1024 - kStagingBytes - kTableBytes - kMiscBytes;
@@ -36,12 +41,21 @@ struct PairLayout {
   static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
+// MX = block-scaled e4m3 (kind::mxf8f6f4): tmSFA / tmSFB view the UE8M0 scales of A and B as
+// [atoms * 2, 256] bytes (512-B atoms of 128 rows x 4 scales, the 128x4 blocked layout: a
+// segment's rows start on a fresh 128-row block, atom (block, K group) at block * K/128 + group).
+template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false, bool MX = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
-                             const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using L = PairLayout<BN>;
+                             const __grid_constant__ CUtensorMap tmC,
+                             const __grid_constant__ CUtensorMap tmSFA,
+                             const __grid_constant__ CUtensorMap tmSFB, const GemmParams p) {
+  using L = PairLayout<BN, MX>;
+  // MX: the scales sit in TMEM columns 448-459, beside the two accumulators (0 and 256, each at
+  // most 192 wide); a 192-row B tile starts 0 or 64 rows into its first 128-row scale block
+  static_assert(!MX || (FP8 && !BMN && BN <= 192 && BN % 64 == 0), "MX tile");
+  constexpr uint32_t kSfaCol = 448, kSfbCol = 452;
   constexpr int S = L::kStages;
   // BN = N of the pair tile = columns of each CTA's accumulator (multiple of 32, <= 256)
   static_assert(BN % 32 == 0 && BN <= 256 && (EPI == kEpiStore || BN % 64 == 0), "tile width");
@@ -60,6 +74,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   int* t_rowoff = t_cnt + kMaxSegments;
   int* t_order = t_rowoff + kMaxSegments;
   int* t_tileoff = t_order + kMaxSegments;
+  int* t_sfoff = t_tileoff + kMaxSegments + 4;  // MX only: first 128-row scale block per segment
   uint8_t* misc = smem + L::kTileBytes + L::kStagingBytes + L::kTableBytes;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(misc);
   uint64_t* empty_bar = full_bar + S;
@@ -103,6 +118,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   build_segment_table<kTileM, kOutBN>(p, tiles, t_cnt, t_rowoff, t_order, t_tileoff,
                                       total_tiles_s, err);
+  if (MX && warp == 1) {  // exclusive prefix sum of 128-row scale blocks, in segment order
+    const int nseg = p.num_segments;
+    int carry = 0;
+    for (int base = 0; base < nseg; base += 32) {
+      const int s = base + lane;
+      const int v = s < nseg ? (t_cnt[s] + 127) / 128 : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (s < nseg) t_sfoff[s] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
@@ -158,7 +189,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint8_t* a_dst = tiles + stage * L::kStageBytes;
             uint8_t* b_dst = a_dst + L::kABytes;
             if (leader) {
-              mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+              mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kTxBytes);
               armed |= 1u << stage;
               armed_par = (armed_par & ~(1u << stage)) | (static_cast<uint32_t>(phase) << stage);
             }
@@ -172,6 +203,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                  info.brow0 + kb * kBK);
             } else {
               tma_load_2d_pair(b_dst, &tmB, fb, kb * kStageK, b_row);
+            }
+            if (MX) {
+              uint8_t* sf_dst = b_dst + L::kBBytes;
+              const int seg = info.seg;
+              const int blk_a = t_sfoff[seg] + (info.row0 - t_rowoff[seg]) / 128 +
+                                static_cast<int>(rank);
+              tma_load_2d_pair(sf_dst, &tmSFA, fb, 0, 2 * (blk_a * num_kb + kb));
+              // both CTAs hold the scales of all the tile's weight rows (the MMA reads B's
+              // scales from each CTA's own TMEM)
+              const int w_row = epi_glu(EPI) ? 2 * info.n0 : info.n0;  // within the expert
+              const int blk_b = (seg % p.num_experts) * ((p.n_b + 127) / 128) + w_row / 128;
+              tma_load_2d_pair(sf_dst + 512, &tmSFB, fb, 0, 2 * (blk_b * num_kb + kb));
+              tma_load_2d_pair(sf_dst + 1024, &tmSFB, fb, 0, 2 * ((blk_b + 1) * num_kb + kb));
             }
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -193,6 +237,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       while (true) {
         if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
         const bool valid = ring[q].rows > 0;
+        const int n0 = ring[q].n0;
         mbar_arrive(&sche_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (!valid) break;
@@ -211,12 +256,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = BMN ? sdesc_sw128_mnmajor(a_addr + L::kABytes, 8192)
                                      : sdesc_sw128_kmajor(a_addr + L::kABytes);
           constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
+          if (MX) {
+            // scales of this stage into TMEM (in order with the MMAs below and the previous
+            // stage's): A's 128 rows, then B's 256 rows as two 4-column atoms
+            const uint32_t sf_addr = a_addr + L::kABytes + L::kBBytes;
+            tmem_cp_32x128b_x4_pair(tmem_base + kSfaCol, sdesc_rows16(sf_addr));
+            tmem_cp_32x128b_x4_pair(tmem_base + kSfbCol, sdesc_rows16(sf_addr + 512));
+            tmem_cp_32x128b_x4_pair(tmem_base + kSfbCol + 4, sdesc_rows16(sf_addr + 1024));
+            // weight row w of the tile has its scales in column (first row % 128 + w) / 32
+            const uint32_t sfb_col =
+                kSfbCol + static_cast<uint32_t>(((epi_glu(EPI) ? 2 * n0 : n0) & 127) >> 5);
+            constexpr uint32_t kIdesc = idesc_mxf8(kTileM, BN);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // K step kk uses scale byte kk of each TMEM word
+              mma_mxf8_ss_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk,
+                               idesc_sf_ids(kIdesc, kk, kk),
+                               (tmem_base + kSfaCol) | (static_cast<uint32_t>(kk) << 30),
+                               (tmem_base + sfb_col) | (static_cast<uint32_t>(kk) << 30),
+                               (kb | kk) != 0);
+          } else {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {  // four 32-byte K steps per 128-byte stage row
             if (FP8)
               mma_f8_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
             else
               mma_f16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + kBStep * kk, idesc, (kb | kk) != 0);
+          }
           }
           mma_commit_pair(&empty_bar[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }

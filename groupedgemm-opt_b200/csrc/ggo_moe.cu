@@ -339,6 +339,102 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------------------------------------------------------- MX (block-scaled) quantisation
+// OCP MX e4m3 with UE8M0 scales, one per 32 consecutive elements of a row. For each group of 32:
+// amax = max |x|, E = floor(log2 amax), scale exponent X = E - 8, plus 1 when amax / 2^E > 1.75
+// (so amax / 2^X <= 448, the largest e4m3 value: nothing clips), clamped to [-127, 127] (a zero
+// group gets -127); q = e4m3 round-to-nearest-even of x * 2^-X (exact power-of-two scaling).
+// Scales go to the 128x4 blocked layout the block-scaled tensor-core MMA reads: segment s's rows
+// start a fresh 128-row block after the blocks of segments < s; block b and K group g (128
+// elements, 4 scales) form the 512-B atom b * K/128 + g, in which row r (0..127) and scale j
+// (0..3) sit at byte (r % 32) * 16 + (r / 32) * 4 + j. Bytes of padding rows are not written.
+constexpr int kMxMaxSegments = 1024;
+
+template <typename T16>
+__global__ void __launch_bounds__(256)
+    quantize_mxfp8_kernel(const T16* __restrict__ x, const int64_t* __restrict__ counts, int nseg,
+                          int rows, int k, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  __shared__ int s_rowoff[kMxMaxSegments + 1];
+  __shared__ int s_blkoff[kMxMaxSegments];
+  if (threadIdx.x < 32) {  // exclusive prefix sums of rows and 128-row blocks, segment order
+    const int lane = threadIdx.x;
+    int carry = 0, bcarry = 0;
+    for (int base = 0; base < nseg; base += 32) {
+      const int s = base + lane;
+      long long c = s < nseg ? counts[s] : 0;
+      c = c < 0 ? 0 : (c > rows ? rows : c);
+      const int v = static_cast<int>(c), b = (v + 127) / 128;
+      int xs = v, ys = b;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int xu = __shfl_up_sync(0xffffffffu, xs, o);
+        const int yu = __shfl_up_sync(0xffffffffu, ys, o);
+        if (lane >= o) {
+          xs += xu;
+          ys += yu;
+        }
+      }
+      if (s < nseg) {
+        s_rowoff[s] = carry + xs - v;
+        s_blkoff[s] = bcarry + ys - b;
+      }
+      carry += __shfl_sync(0xffffffffu, xs, 31);
+      bcarry += __shfl_sync(0xffffffffu, ys, 31);
+    }
+    if (lane == 0) s_rowoff[nseg] = carry;
+  }
+  __syncthreads();
+  const int ng = k / 32, kg = k / 128;
+  const int covered = s_rowoff[nseg];
+  const long long total = static_cast<long long>(rows) * ng;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * 256) {
+    const int r = static_cast<int>(i / ng), j = static_cast<int>(i % ng);
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * k + j * 32);
+    float f[32];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float g[8];
+      unpack8<T16>(src[u], g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[8 * u + e] = g[e];
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    const uint32_t bits = __float_as_uint(amax);
+    const int eb = static_cast<int>((bits >> 23) & 0xFFu);
+    int xe = eb == 0 ? -127 : eb - 127 - 8 + ((bits & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+    xe = xe < -127 ? -127 : (xe > 127 ? 127 : xe);
+    const float inv = xe <= 126 ? __uint_as_float(static_cast<uint32_t>(127 - xe) << 23)
+                                : __uint_as_float(1u << 22);  // 2^-127
+    uint32_t w[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+          make_float2(f[4 * h] * inv, f[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+      const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+          make_float2(f[4 * h + 2] * inv, f[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+      w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(q + static_cast<size_t>(r) * k + j * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (r < covered) {
+      int lo = 0, hi = nseg - 1;  // the last segment starting at or before r is r's segment
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_rowoff[mid] <= r) lo = mid; else hi = mid - 1;
+      }
+      const int rl = r - s_rowoff[lo];
+      const int blk = s_blkoff[lo] + rl / 128;
+      const int rr = rl & 127;
+      sf[(static_cast<size_t>(blk) * kg + j / 4) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (j & 3)] =
+          static_cast<uint8_t>(xe + 127);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- expert-parallel signalling
 // Each rank owns an IPC-shared sync board: counts [kMaxPeers][E] int64 (every rank's
 // tokens_per_expert, written by that rank) and flags [kEpSlots][kMaxPeers] int64 (per phase, the
@@ -525,6 +621,32 @@ int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dty
     ggo::quantize_rows_fp8_kernel<__half><<<grid, 256, 0, stream>>>(
         static_cast<const __half*>(x_dev), static_cast<int>(rows), static_cast<int>(cols),
         static_cast<uint8_t*>(q_dev), scale_dev);
+  return ggo::check_launch();
+}
+
+int ggo_quantize_mxfp8(const void* x_dev, int dtype, const int64_t* counts_dev, int num_segments,
+                       int64_t rows, int64_t k, void* q_dev, void* scale_dev,
+                       cudaStream_t stream) {
+  if (!x_dev || !counts_dev || !q_dev || !scale_dev || rows < 0 || k <= 0)
+    return GGO_ERR_INVALID_ARG;
+  if (num_segments <= 0) return GGO_ERR_INVALID_ARG;
+  if (num_segments > ggo::kMxMaxSegments) return GGO_ERR_TOO_MANY_SEGMENTS;
+  if (dtype != GGO_DTYPE_BF16 && dtype != GGO_DTYPE_FP16) return GGO_ERR_DTYPE;
+  if (k % 128 || !ggo::aligned16(x_dev) || !ggo::aligned16(q_dev)) return GGO_ERR_ALIGNMENT;
+  if (rows > INT32_MAX || k > INT32_MAX) return GGO_ERR_SHAPE;
+  if (rows == 0) return GGO_OK;
+  const long long groups = rows * (k / 32);
+  const long long want = (groups + 255) / 256;
+  const int grid = static_cast<int>(want < 4096 ? want : 4096);
+  if (dtype == GGO_DTYPE_BF16)
+    ggo::quantize_mxfp8_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x_dev), counts_dev, num_segments,
+        static_cast<int>(rows), static_cast<int>(k), static_cast<uint8_t*>(q_dev),
+        static_cast<uint8_t*>(scale_dev));
+  else
+    ggo::quantize_mxfp8_kernel<__half><<<grid, 256, 0, stream>>>(
+        static_cast<const __half*>(x_dev), counts_dev, num_segments, static_cast<int>(rows),
+        static_cast<int>(k), static_cast<uint8_t*>(q_dev), static_cast<uint8_t*>(scale_dev));
   return ggo::check_launch();
 }
 

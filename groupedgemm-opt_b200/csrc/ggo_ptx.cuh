@@ -343,6 +343,51 @@ __device__ __forceinline__ void mma_f8_ss_pair(uint32_t tmem_d, uint64_t adesc, 
       : "memory");
 }
 
+// ---------------------------------------------------------------- block-scaled (MX) operands
+// Instruction descriptor for tcgen05.mma kind::mxf8f6f4.block_scale with e4m3 A and B (format 0),
+// K-major operands and UE8M0 scale factors (bit 23). The accumulator is always fp32 here, so bits
+// 4-5 carry B's scale-factor byte index and bits 29-30 A's (which byte of the 32-bit TMEM word
+// holds the scales of this 32-deep K step).
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n) {
+  return (1u << 23) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_sf_ids(uint32_t idesc, uint32_t a_id, uint32_t b_id) {
+  return idesc | (a_id << 29) | (b_id << 4);
+}
+
+// Shared-memory descriptor of a tcgen05.cp source: 32 rows of 16 bytes, contiguous, no swizzle
+// (core matrices of 8 rows x 16 B, 128 B apart along the rows).
+__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(128 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;  // layout type 0: no swizzle
+}
+
+// Copy 32 rows x 128 bits of shared memory into TMEM lanes 0-31 of 4 consecutive columns and
+// replicate them into the other three lane quarters; in a CTA pair each CTA copies its own shared
+// memory into its own TMEM. Ordered with later tcgen05.mma of the same thread.
+__device__ __forceinline__ void tmem_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// D[tmem] (+)= (A * 2^sfa) * (B * 2^sfb)^T over one 32-deep K step, CTA pair, e4m3 operands with
+// one UE8M0 scale per row per 32 K elements read from TMEM (`sfa`, `sfb`: column addresses whose
+// top two bits select the byte, the same byte indices as the descriptor's).
+__device__ __forceinline__ void mma_mxf8_ss_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
 // Arrive once on the barrier at the same shared offset in every CTA of `cta_mask` when all
 // tcgen05 ops issued so far by this thread have completed.
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {

@@ -228,6 +228,87 @@ torch::Tensor grouped_gemm_swiglu_fp8(const torch::Tensor& x_q, const torch::Ten
   return h;
 }
 
+// MX quantisation of x [..., K] whose rows form segments of `counts` rows: returns (q
+// float8_e4m3fn, same shape, UE8M0 scales uint8 [ggo_mxfp8_scale_bytes] in the blocked layout;
+// padding bytes zero).
+std::tuple<torch::Tensor, torch::Tensor> quantize_mxfp8(const torch::Tensor& x,
+                                                        const torch::Tensor& counts) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.dim() >= 2, "x must be contiguous CUDA");
+  c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t k = x.size(-1), rows = x.numel() / k;
+  auto c = counts_on_device(counts, x.device());
+  const int nseg = static_cast<int>(c.numel());
+  const size_t sb = ggo_mxfp8_scale_bytes(rows, nseg, k);
+  TORCH_CHECK(sb > 0 || rows == 0, "K must be a multiple of 128");
+  auto q = torch::empty(x.sizes(), x.options().dtype(torch::kFloat8_e4m3fn));
+  auto sf = torch::zeros({static_cast<int64_t>(sb)}, x.options().dtype(torch::kUInt8));
+  check_status(ggo_quantize_mxfp8(x.data_ptr(), dtype_code(x), c.data_ptr<int64_t>(), nseg, rows,
+                                  k, q.data_ptr(), sf.data_ptr(), stream),
+               "mxfp8 quantisation");
+  return {q, sf};
+}
+
+void check_mx_operands(const torch::Tensor& a_q, const torch::Tensor& a_sf,
+                       const torch::Tensor& w_q, const torch::Tensor& w_sf, int64_t nseg) {
+  TORCH_CHECK(a_q.is_cuda() && w_q.is_cuda() && a_q.dim() == 2 && w_q.dim() == 3,
+              "a_q [T, K] and w_q [E, N, K] CUDA tensors");
+  TORCH_CHECK(a_q.scalar_type() == torch::kFloat8_e4m3fn &&
+                  w_q.scalar_type() == torch::kFloat8_e4m3fn, "operands must be float8_e4m3fn");
+  TORCH_CHECK(a_q.size(1) == w_q.size(2), "K mismatch");
+  TORCH_CHECK(a_q.is_contiguous() && w_q.is_contiguous() && a_sf.is_contiguous() &&
+                  w_sf.is_contiguous(), "operands must be contiguous");
+  TORCH_CHECK(a_sf.scalar_type() == torch::kUInt8 && w_sf.scalar_type() == torch::kUInt8,
+              "scales must be uint8 (UE8M0)");
+  const int64_t T = a_q.size(0), K = a_q.size(1), E = w_q.size(0), N = w_q.size(1);
+  TORCH_CHECK(a_sf.numel() >= static_cast<int64_t>(ggo_mxfp8_scale_bytes(T, nseg, K)),
+              "input scales smaller than ggo_mxfp8_scale_bytes(T, segments, K)");
+  TORCH_CHECK(w_sf.numel() >= E * ((N + 127) / 128) * (K / 128) * 512,
+              "weight scales smaller than E * ceil(N / 128) * K / 128 atoms");
+}
+
+// MXFP8 grouped GEMM: out bf16 [T, N].
+torch::Tensor grouped_gemm_mxfp8(const torch::Tensor& a_q, const torch::Tensor& a_sf,
+                                 const torch::Tensor& w_q, const torch::Tensor& w_sf,
+                                 const torch::Tensor& counts, int64_t num_experts,
+                                 bool sort_by_m) {
+  check_mx_operands(a_q, a_sf, w_q, w_sf, counts.numel());
+  c10::cuda::CUDAGuard guard(a_q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = a_q.size(0), K = a_q.size(1), N = w_q.size(1);
+  auto out = torch::empty({T, N}, a_q.options().dtype(torch::kBFloat16));
+  if (T == 0) return out;
+  auto c = counts_on_device(counts, a_q.device());
+  const int st = ggo_grouped_gemm_mxfp8(
+      a_q.data_ptr(), a_sf.data_ptr(), w_q.data_ptr(), w_sf.data_ptr(), out.data_ptr(),
+      c.data_ptr<int64_t>(), static_cast<int>(c.numel()), static_cast<int>(num_experts), T, N, K,
+      sort_by_m ? 1 : 0, workspace_for(a_q.device(), stream), stream);
+  check_status(st, "mxfp8 grouped GEMM");
+  return out;
+}
+
+// MXFP8 gate/up SwiGLU grouped GEMM over the blocked gate/up weight [E, glu_rows(F), K]: h [T, F].
+torch::Tensor grouped_gemm_swiglu_mxfp8(const torch::Tensor& x_q, const torch::Tensor& x_sf,
+                                        const torch::Tensor& w_q, const torch::Tensor& w_sf,
+                                        const torch::Tensor& counts, int64_t num_experts,
+                                        int64_t F, bool sort_by_m) {
+  check_mx_operands(x_q, x_sf, w_q, w_sf, counts.numel());
+  TORCH_CHECK(F > 0 && w_q.size(1) == ggo_mxfp8_glu_rows(F),
+              "w_q must be the blocked gate/up weight [E, ggo_mxfp8_glu_rows(F), K]");
+  c10::cuda::CUDAGuard guard(x_q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t T = x_q.size(0), K = x_q.size(1);
+  auto h = torch::empty({T, F}, x_q.options().dtype(torch::kBFloat16));
+  if (T == 0) return h;
+  auto c = counts_on_device(counts, x_q.device());
+  const int st = ggo_grouped_gemm_swiglu_mxfp8(
+      x_q.data_ptr(), x_sf.data_ptr(), w_q.data_ptr(), w_sf.data_ptr(), h.data_ptr(),
+      c.data_ptr<int64_t>(), static_cast<int>(c.numel()), static_cast<int>(num_experts), T, F, K,
+      sort_by_m ? 1 : 0, workspace_for(x_q.device(), stream), stream);
+  check_status(st, "mxfp8 gate/up SwiGLU grouped GEMM");
+  return h;
+}
+
 torch::Tensor grouped_gemm_swiglu(const torch::Tensor& x, const torch::Tensor& w_gate_up,
                                   const torch::Tensor& counts, int64_t num_experts,
                                   bool sort_by_m) {
@@ -573,6 +654,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm_wgrad", &grouped_gemm_wgrad, py::arg("x"), py::arg("dy"),
         py::arg("tokens_per_expert"), py::arg("sort_by_m") = true);
   m.def("quantize_fp8_rows", &quantize_fp8_rows, py::arg("x"));
+  m.def("quantize_mxfp8", &quantize_mxfp8, py::arg("x"), py::arg("counts"));
+  m.def("grouped_gemm_mxfp8", &grouped_gemm_mxfp8, py::arg("input_q"), py::arg("input_scale"),
+        py::arg("weights_q"), py::arg("weight_scale"), py::arg("counts"), py::arg("num_experts"),
+        py::arg("sort_by_m") = true);
+  m.def("grouped_gemm_swiglu_mxfp8", &grouped_gemm_swiglu_mxfp8, py::arg("x_q"),
+        py::arg("x_scale"), py::arg("w_q"), py::arg("w_scale"), py::arg("counts"),
+        py::arg("num_experts"), py::arg("F"), py::arg("sort_by_m") = true);
+  m.def("mxfp8_glu_rows", [](int64_t f) { return ggo_mxfp8_glu_rows(f); });
+  m.def("mxfp8_scale_bytes", [](int64_t rows, int64_t nseg, int64_t k) {
+    return static_cast<int64_t>(ggo_mxfp8_scale_bytes(rows, static_cast<int>(nseg), k));
+  });
   m.def("grouped_gemm_swiglu_fp8", &grouped_gemm_swiglu_fp8, py::arg("x_q"), py::arg("x_scale"),
         py::arg("w_gate_up_q"), py::arg("w_scale"), py::arg("tokens_per_segment"),
         py::arg("num_experts"), py::arg("sort_by_m") = true);

@@ -287,3 +287,41 @@ def fused_moe_fp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: Mo
     hq, hsc = _C.quantize_fp8_rows(h)
     y = _C.grouped_gemm_fp8(hq, hsc, weights.w_down_q, weights.w_down_scale, tpe, 4, sort_by_m)
     return _C.moe_combine(y, w, slot_pos)
+
+
+@dataclass
+class MoEMXFP8Weights:
+    """MXFP8 expert weights (see quantize_moe_weights_mxfp8): e4m3 with UE8M0 block scales."""
+    w_gate_up_q: torch.Tensor      # [E, 2 F_pad, H] float8_e4m3fn, blocked gate/up rows
+    w_gate_up_scale: torch.Tensor  # uint8, 128x4 blocked scale layout
+    w_down_q: torch.Tensor         # [E, H, F] float8_e4m3fn
+    w_down_scale: torch.Tensor     # uint8
+    F: int
+
+
+def quantize_moe_weights_mxfp8(w_gate_up: torch.Tensor, w_down: torch.Tensor) -> MoEMXFP8Weights:
+    """MX quantisation of the layer's weights (once, on the GPU); the gate/up weight is first
+    reordered into the blocked layout of the MXFP8 SwiGLU GEMM."""
+    from grouped_gemm_opt.ops import mxfp8_block_gate_up, quantize_mxfp8
+    gq, gs = quantize_mxfp8(mxfp8_block_gate_up(w_gate_up))
+    dq, ds = quantize_mxfp8(w_down)
+    return MoEMXFP8Weights(gq, gs, dq, ds, w_gate_up.size(1) // 2)
+
+
+def fused_moe_mxfp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: MoEMXFP8Weights,
+                    top_k: int, sort_by_m: bool = True) -> torch.Tensor:
+    """Single-GPU MoE layer with MXFP8 grouped GEMMs: route -> dispatch -> MX quantisation of the
+    gathered rows -> gate/up GEMM with the SwiGLU epilogue (bf16 h) -> MX quantisation of h ->
+    down GEMM -> combine. Routing, dispatch and combine are the bf16 layer's."""
+    from grouped_gemm_opt._native import _C
+    E = router_logits.size(1)
+    assert weights.w_gate_up_q.size(0) == E, "all experts must be local"
+    ids, w, tpe, scratch = _C.moe_route(router_logits, top_k)
+    xs, _, slot_pos = _C.moe_permute(hidden.contiguous(), ids, scratch, E)
+    xq, xsc = _C.quantize_mxfp8(xs, tpe)
+    h = _C.grouped_gemm_swiglu_mxfp8(xq, xsc, weights.w_gate_up_q, weights.w_gate_up_scale, tpe,
+                                     E, weights.F, sort_by_m)
+    hq, hsc = _C.quantize_mxfp8(h, tpe)
+    y = _C.grouped_gemm_mxfp8(hq, hsc, weights.w_down_q, weights.w_down_scale, tpe, E, sort_by_m)
+    return _C.moe_combine(y, w, slot_pos)
+

@@ -167,3 +167,60 @@ def grouped_gemm_opt_fp8(
     return _C.grouped_gemm_fp8(input_q.contiguous(), input_scale.contiguous().float(),
                                weights_q.contiguous(), weight_scale.contiguous().float(),
                                tokens_per_expert, int(tile_config), sort_by_m)
+
+
+def quantize_mxfp8(x: torch.Tensor, tokens_per_expert: torch.Tensor = None):
+    """MX (OCP microscaling) e4m3 quantisation on the GPU: every 32 consecutive elements of a row
+    share one UE8M0 scale 2^(byte - 127). Returns (q float8_e4m3fn, scales uint8) with the scales
+    in the 128x4 blocked layout the block-scaled tensor cores read, each expert's rows starting a
+    fresh 128-row block. Activations [T, K]: pass ``tokens_per_expert`` (the rows are
+    expert-sorted). Weights [E, N, K]: leave it None (E segments of N rows). K % 128 == 0."""
+    x = x.contiguous()
+    if tokens_per_expert is None:
+        assert x.dim() == 3, "weights [E, N, K] when tokens_per_expert is None"
+        counts = torch.full((x.size(0),), x.size(1), dtype=torch.int64, device=x.device)
+    else:
+        counts = tokens_per_expert.to(torch.int64)
+    return _C.quantize_mxfp8(x, counts)
+
+
+def grouped_gemm_opt_mxfp8(
+    input_q: torch.Tensor,
+    input_scale: torch.Tensor,
+    weights_q: torch.Tensor,
+    weight_scale: torch.Tensor,
+    tokens_per_expert: torch.Tensor,
+    sort_by_m: bool = True,
+) -> torch.Tensor:
+    """MXFP8 grouped GEMM: ``out[i] = sum_k (q_in[i,k] 2^s_in[i,k//32]) (q_w[e,n,k] 2^s_w[e,n,k//32])``
+    in bf16, the block scales applied by the tensor cores (tcgen05 kind::mxf8f6f4.block_scale,
+    fp32 accumulation). Operands and scales come from :func:`quantize_mxfp8` (the input quantised
+    with the same ``tokens_per_expert``)."""
+    assert input_q.is_cuda and weights_q.is_cuda
+    tokens_per_expert = tokens_per_expert.to(torch.int64).contiguous()
+    if not tokens_per_expert.is_cuda:
+        total = int(tokens_per_expert.sum().item())
+        assert total == input_q.size(0), (
+            f"sum(tokens_per_expert)={total} != total_tokens={input_q.size(0)}")
+    return _C.grouped_gemm_mxfp8(input_q.contiguous(), input_scale.contiguous(),
+                                 weights_q.contiguous(), weight_scale.contiguous(),
+                                 tokens_per_expert, weights_q.size(0), sort_by_m)
+
+
+def mxfp8_block_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
+    """Reorders a gate/up weight [E, 2F, K] (gate rows then up rows) into the blocked layout the
+    MXFP8 SwiGLU GEMM reads: [E, 2 * F_pad, K], F_pad = F rounded up to 96, block j = gate rows
+    96j..96j+95 then the matching up rows, zero rows past F. A one-time weight preparation."""
+    E, two_f, K = w_gate_up.shape
+    F = two_f // 2
+    rows = _C.mxfp8_glu_rows(F)
+    fp = rows // 2
+    out = w_gate_up.new_zeros(E, fp // 96, 2, 96, K)
+    g = w_gate_up.new_zeros(E, fp, K)
+    g[:, :F] = w_gate_up[:, :F]
+    out[:, :, 0] = g.view(E, fp // 96, 96, K)
+    g.zero_()
+    g[:, :F] = w_gate_up[:, F:]
+    out[:, :, 1] = g.view(E, fp // 96, 96, K)
+    return out.view(E, rows, K)
+

@@ -157,6 +157,52 @@ int ggo_grouped_gemm_swiglu_fp8(const void* x_dev, const float* x_scale_dev,
 int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dtype, void* q_dev,
                           float* scale_dev, cudaStream_t stream);
 
+/* MXFP8: block-scaled e4m3 (OCP MX; no reference counterpart). Every 32 consecutive K elements
+ * of a row share one UE8M0 scale 2^(byte - 127); the tensor cores apply both operands' scales
+ * (tcgen05 kind::mxf8f6f4.block_scale) and accumulate in fp32.
+ * Scale layout ("128x4 blocked"): the rows of each segment start a fresh 128-row block after the
+ * blocks of the previous segments; block b and K group g (128 elements, 4 scales) form the 512-B
+ * atom at byte (b * K/128 + g) * 512, inside which row r (0..127) and scale j (0..3) of the group
+ * sit at byte (r % 32) * 16 + (r / 32) * 4 + j. Weights [E, N, K] are E segments of N rows. */
+
+/* Bytes of the scale buffer for `rows` rows in `num_segments` segments, K columns (an upper bound
+ * that needs no counts: ceil(rows / 128) + num_segments blocks). 0 if K is not a multiple of 128. */
+size_t ggo_mxfp8_scale_bytes(int64_t rows, int num_segments, int64_t k);
+
+/* MX quantisation of a bf16/fp16 matrix [rows, k] whose rows form consecutive segments of
+ * counts_dev[s] rows (device int64; weights: num_segments = E, every count N). Per 32-element
+ * group: X = floor(log2 amax) - 8, plus 1 when amax / 2^floor(log2 amax) > 1.75, clamped to
+ * [-127, 127] (-127 for an all-zero group); scale byte X + 127; q = e4m3(x * 2^-X), round to
+ * nearest even. q_dev [rows, k] e4m3 bytes; scale_dev ggo_mxfp8_scale_bytes() bytes (padding
+ * bytes are left as they were). k a multiple of 128, at most 1024 segments. */
+int ggo_quantize_mxfp8(const void* x_dev, int dtype, const int64_t* counts_dev, int num_segments,
+                       int64_t rows, int64_t k, void* q_dev, void* scale_dev,
+                       cudaStream_t stream);
+
+/* MXFP8 grouped GEMM: out[r, n] = sum_k (a[r,k] 2^sa[r,k/32]) (b[e,n,k] 2^sb[e,n,k/32]) in bf16.
+ * input_dev [T, K] and weights_dev [E, N, K] e4m3 with their scales from ggo_quantize_mxfp8
+ * (the input quantised with these same segment counts). Segment s multiplies expert
+ * s % num_experts. K a multiple of 128, N of 8. Runs 256 x 192 CTA-pair tiles. */
+int ggo_grouped_gemm_mxfp8(const void* input_dev, const void* input_scale_dev,
+                           const void* weights_dev, const void* weight_scale_dev, void* output_dev,
+                           const int64_t* tokens_per_segment_dev, int num_segments,
+                           int num_experts, int64_t total_tokens, int64_t N, int64_t K,
+                           int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
+/* Rows per expert of the blocked gate/up weight the MXFP8 SwiGLU GEMM reads: 2 * F_pad with
+ * F_pad = F rounded up to 96. Block j (rows 192j .. 192j+191) holds gate rows 96j .. 96j+95 then
+ * the matching up rows; rows past F are zero. */
+int64_t ggo_mxfp8_glu_rows(int64_t F);
+
+/* MXFP8 gate/up GEMM with the SwiGLU epilogue: h[r, f] = silu(g) * u, g / u the block-scaled
+ * products of x row r with gate / up row f. w_gate_up_dev [E, ggo_mxfp8_glu_rows(F), K] e4m3 in the
+ * blocked layout above, quantised as E segments of ggo_mxfp8_glu_rows(F) rows. h_dev [T, F] bf16. */
+int ggo_grouped_gemm_swiglu_mxfp8(const void* x_dev, const void* x_scale_dev,
+                                  const void* w_gate_up_dev, const void* w_scale_dev, void* h_dev,
+                                  const int64_t* tokens_per_segment_dev, int num_segments,
+                                  int num_experts, int64_t total_tokens, int64_t F, int64_t K,
+                                  int sort_by_m, void* workspace_dev, cudaStream_t stream);
+
 /* Fused-MoE stage 2: gate/up grouped GEMM with the SwiGLU epilogue.
  *   h[r, f] = silu(x[r,:] . Wgu[e, f, :]) * (x[r,:] . Wgu[e, F + f, :])
  * w_gate_up_dev [num_experts, 2F, K]: rows 0..F-1 gate, rows F..2F-1 up.

@@ -19,6 +19,13 @@ jeshxxx/GroupedGEMM-OPT):
                            grouped_gemm_opt/moe.py. Parity of these stages is UNPINNED (no
                            reference implementation exists to pin against).
 
+  mx_quantize / mx_dequantize / mx_block_gate_up   MXFP8 (block-scaled e4m3). The reference is
+                           bf16/fp16 only, so these restate the OCP Microscaling (MX) v1.0 format
+                           (32-element blocks, UE8M0 scales) and the 128x4 blocked scale layout
+                           of block-scaled tcgen05 MMAs, with the scale-exponent rule the library
+                           documents in include/ggo.h. UNPINNED to the reference (it has no
+                           counterpart); checked by known-answer vectors in tests/test_oracle.py.
+
 Pinning: ``sequential_gemm`` and the two distribution generators are checked against golden
 vectors produced by the reference's own benchmark.py (tests/golden/make_golden.py imports it and
 commits small fixtures); see tests/test_oracle.py.
@@ -164,3 +171,92 @@ def moe_layer(hidden: torch.Tensor, logits: torch.Tensor, w_gate_up: torch.Tenso
     if round_to is not None:
         y = y.to(round_to)
     return combine(y, w, slot_pos)
+
+
+# ----------------------------------------------------------------------------- MXFP8
+def mx_scale_exponent(amax: np.ndarray) -> np.ndarray:
+    """Shared exponent X of 32-element groups from their fp32 amax: floor(log2 amax) - 8, plus 1
+    when amax / 2^floor(log2 amax) > 1.75 (so amax / 2^X <= 448 = max e4m3), clamped to
+    [-127, 127]; -127 for amax == 0 (and for fp32 subnormals). Pure bit arithmetic."""
+    bits = np.asarray(amax, dtype=np.float32).view(np.uint32).astype(np.int64)
+    eb = (bits >> 23) & 0xFF
+    mant = bits & 0x7FFFFF
+    x = np.where(eb == 0, -127, eb - 127 - 8 + (mant > 0x600000).astype(np.int64))
+    return np.clip(x, -127, 127)
+
+
+def mx_atom_offset(block: np.ndarray, r: np.ndarray, group: np.ndarray, k: int) -> np.ndarray:
+    """Byte offset of the scale of row r (0..127) of 128-row block `block`, 32-element group
+    `group` in the 128x4 blocked layout: atom (block * K/128 + group // 4), byte
+    (r % 32) * 16 + (r // 32) * 4 + group % 4."""
+    return ((block * (k // 128) + group // 4) * 512 + (r % 32) * 16 + (r // 32) * 4 + group % 4)
+
+
+def mx_quantize(x: torch.Tensor, counts) -> tuple:
+    """MX e4m3 quantisation of x [rows, K] (rows in consecutive segments of `counts` rows).
+    Returns (q uint8 [rows, K] e4m3 bit patterns, scales uint8 [(ceil(rows/128) + nseg) * K/128
+    * 512], padding bytes 0). e4m3 rounding is torch's round-to-nearest-even float8 cast of the
+    exactly scaled fp32 values (none exceeds 448, so no saturation is involved)."""
+    xf = x.float().contiguous()
+    rows, k = xf.shape
+    assert k % 128 == 0
+    g = xf.view(rows, k // 32, 32)
+    amax = g.abs().amax(dim=-1).numpy()
+    xe = mx_scale_exponent(amax)                                      # [rows, K/32]
+    inv = torch.from_numpy(np.ldexp(np.float32(1.0), -xe).astype(np.float32))
+    q = (g * inv.unsqueeze(-1)).view(rows, k).to(torch.float8_e4m3fn).view(torch.uint8)
+    counts = np.minimum(np.maximum(np.asarray(counts, dtype=np.int64), 0), rows)
+    nseg = counts.size
+    sf = np.zeros(((rows + 127) // 128 + nseg) * (k // 128) * 512, dtype=np.uint8)
+    rowoff = np.concatenate([[0], np.cumsum(counts)])
+    blkoff = np.concatenate([[0], np.cumsum((counts + 127) // 128)])
+    groups = np.arange(k // 32)
+    for s_ in range(nseg):
+        for rl in range(int(counts[s_])):
+            r = rowoff[s_] + rl
+            if r >= rows:
+                break
+            off = mx_atom_offset(blkoff[s_] + rl // 128, rl % 128, groups, k)
+            sf[off] = (xe[r] + 127).astype(np.uint8)
+    return q, sf
+
+
+def mx_dequantize(q: torch.Tensor, sf: np.ndarray, counts, k: int) -> torch.Tensor:
+    """fp32 values q * 2^(scale - 127) of MX data laid out as mx_quantize writes it."""
+    qf = q.view(torch.float8_e4m3fn).float().view(-1, k)
+    rows = qf.size(0)
+    counts = np.minimum(np.maximum(np.asarray(counts, dtype=np.int64), 0), rows)
+    rowoff = np.concatenate([[0], np.cumsum(counts)])
+    blkoff = np.concatenate([[0], np.cumsum((counts + 127) // 128)])
+    scale = np.ones((rows, k // 32), dtype=np.float32)
+    groups = np.arange(k // 32)
+    for s_ in range(counts.size):
+        for rl in range(int(counts[s_])):
+            r = rowoff[s_] + rl
+            off = mx_atom_offset(blkoff[s_] + rl // 128, rl % 128, groups, k)
+            scale[r] = np.ldexp(np.float32(1.0), sf[off].astype(np.int64) - 127)
+    return (qf.view(rows, k // 32, 32) * torch.from_numpy(scale).unsqueeze(-1)).view(rows, k)
+
+
+def mx_block_gate_up(w_gate_up: torch.Tensor, block: int = 96) -> torch.Tensor:
+    """[E, 2F, K] gate-then-up rows -> [E, 2 F_pad, K] blocked: block j = gate rows
+    block*j.. then the matching up rows, zero rows past F (F_pad = F rounded up to `block`)."""
+    E, two_f, K = w_gate_up.shape
+    f = two_f // 2
+    fp = -(-f // block) * block
+    gate = torch.zeros(E, fp, K, dtype=w_gate_up.dtype)
+    up = torch.zeros(E, fp, K, dtype=w_gate_up.dtype)
+    gate[:, :f] = w_gate_up[:, :f]
+    up[:, :f] = w_gate_up[:, f:]
+    out = torch.stack([gate.view(E, fp // block, block, K), up.view(E, fp // block, block, K)], 2)
+    return out.reshape(E, 2 * fp, K)
+
+
+def mx_unblock_gate_up(w_blocked: torch.Tensor, f: int, block: int = 96) -> torch.Tensor:
+    """Inverse of mx_block_gate_up: [E, 2 F_pad, K] blocked -> [E, 2F, K] gate-then-up."""
+    E, rows, K = w_blocked.shape
+    v = w_blocked.reshape(E, rows // (2 * block), 2, block, K)
+    gate = v[:, :, 0].reshape(E, -1, K)[:, :f]
+    up = v[:, :, 1].reshape(E, -1, K)[:, :f]
+    return torch.cat([gate, up], 1)
+

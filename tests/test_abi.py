@@ -77,6 +77,31 @@ def test_moe_validation(lib):
     assert f(None, 16, 8, 2, p, p, p, p, None) == 1
 
 
+def test_mxfp8_metadata_and_validation(lib):
+    lib.ggo_mxfp8_scale_bytes.restype = ctypes.c_size_t
+    lib.ggo_mxfp8_scale_bytes.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int64]
+    assert lib.ggo_mxfp8_scale_bytes(256, 2, 512) == (2 + 2) * 4 * 512
+    assert lib.ggo_mxfp8_scale_bytes(256, 2, 100) == 0   # K must be a multiple of 128
+    lib.ggo_mxfp8_glu_rows.restype = ctypes.c_int64
+    lib.ggo_mxfp8_glu_rows.argtypes = [ctypes.c_int64]
+    assert lib.ggo_mxfp8_glu_rows(200) == 576 and lib.ggo_mxfp8_glu_rows(192) == 384
+    q = lib.ggo_quantize_mxfp8
+    q.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                  ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    p = 1 << 20
+    assert q(None, 0, p, 1, 16, 128, p, p, None) == 1
+    assert q(p, 0, p, 1, 16, 100, p, p, None) == 4      # K % 128
+    assert q(p, 7, p, 1, 16, 128, p, p, None) == 3      # dtype
+    assert q(p, 0, p, 2000, 16, 128, p, p, None) == 5   # too many segments
+    assert q(p, 0, p, 1, 0, 128, p, p, None) == 0       # nothing to do
+    g = lib.ggo_grouped_gemm_mxfp8
+    g.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_int] + \
+        [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    assert g(p, p, p, p, p, p, 8, 8, 256, 1024, 64, 1, p, None) == 4   # K % 128
+    assert g(p, None, p, p, p, p, 8, 8, 256, 1024, 128, 1, p, None) == 1
+    assert g(p, p + 8, p, p, p, p, 8, 8, 256, 1024, 128, 1, p, None) == 4  # scale alignment
+
+
 C_PROGRAM = r"""
 #include <stdio.h>
 #include <string.h>

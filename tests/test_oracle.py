@@ -133,3 +133,48 @@ def test_reference_triton_fused_moe_bug_is_not_reproduced():
             assert dev > 0.1, dev
         else:
             assert dev < 1e-4, (name, dev)
+
+
+# ----------------------------------------------------------------------------- MXFP8 oracle
+def test_mx_scale_exponent_known_answers():
+    """X = floor(log2 amax) - 8, +1 above 1.75 * 2^floor, clamped; zero groups -127."""
+    amax = np.array([448, 449, 1, 0, 1.75, 1.7500001, 2.0 ** -130, 3e38, 2.0 ** -119],
+                    dtype=np.float32)
+    assert oracle.mx_scale_exponent(amax).tolist() == [0, 1, -8, -127, -8, -7, -127, 120, -127]
+
+
+def test_mx_quantize_known_answers():
+    x = torch.zeros(130, 128)
+    x[0, :3] = torch.tensor([448.0, 1.0, -0.5])    # group 0 of row 0: X = 0, exact
+    x[129, 64:67] = torch.tensor([450.0, 226.0, 232.0])  # group 2 of row 129: X = 1
+    q, sf = oracle.mx_quantize(x.to(torch.bfloat16), [130])
+    assert q[0, :3].tolist() == [0x7E, 0x38, 0xB0]  # e4m3 bits of 448, 1, -0.5
+    # 225 -> 224, 113 -> 112, and the tie 116 -> 112 (nearest even)
+    assert q[129, 64:67].tolist() == [0x76, 0x6E, 0x6E]
+    assert sf.size == (2 + 1) * 1 * 512
+    assert sf[0] == 127 and sf[(1 * 1 + 0) * 512 + 1 * 16 + 0 * 4 + 2] == 128
+    assert sf[1] == 0  # an all-zero group: X = -127
+    # padding rows of the second block keep zero bytes
+    assert sf[512 + 2 * 16] == 0
+
+
+def test_mx_round_trip_error_bound():
+    """|dequant(quant(x)) - x| <= max(|x| / 16, half an e4m3 subnormal step) per element."""
+    g = torch.Generator().manual_seed(3)
+    counts = [100, 0, 150, 50]
+    x = (torch.randn(300, 256, generator=g) * torch.logspace(-3, 3, 300).unsqueeze(1)).to(
+        torch.bfloat16)
+    q, sf = oracle.mx_quantize(x, counts)
+    d = oracle.mx_dequantize(q, sf, counts, 256)
+    xf = x.float()
+    xe = oracle.mx_scale_exponent(xf.view(300, 8, 32).abs().amax(-1).numpy())
+    step = torch.from_numpy(np.ldexp(1.0, xe - 10).astype(np.float32)).repeat_interleave(32, 1)
+    assert bool(((d - xf).abs() <= torch.maximum(xf.abs() / 16, step)).all())
+
+
+def test_mx_gate_up_blocking_round_trip():
+    w = torch.randn(3, 2 * 200, 128)
+    b = oracle.mx_block_gate_up(w)
+    assert b.shape == (3, 2 * 288, 128)
+    assert torch.equal(b[:, 96:192], w[:, 200:296])  # block 0: gate rows 0..95 then up rows 0..95
+    assert torch.equal(oracle.mx_unblock_gate_up(b, 200), w)
