@@ -307,7 +307,8 @@ def moe_layer_bench(world, rank, steps, warmup):
 
 def profile_run(args):
     """`--profile gemm`: cfg2 grouped GEMM launches only (1 kernel per step).
-    `--profile fp8|dgrad|wgrad`: the FP8 forward / backward kernels on the cfg2 shapes.
+    `--profile fp8|mxfp8|dgrad|wgrad`: the FP8 / MXFP8 forward and the backward kernels on the
+    cfg2 shapes.
     `--profile moe`: the single-GPU Mixtral layer (route, scan, permute, gate/up, down, combine).
     Used under ncu; prints nothing but a done line."""
     import torch
@@ -319,8 +320,9 @@ def profile_run(args):
         w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
         tpe = torch.full((E,), T_TOK // E, dtype=torch.int64, device="cuda")
         fn = lambda: ggo.grouped_gemm_opt(x, w, tpe)  # noqa: E731
-    elif args.profile in ("fp8", "dgrad", "wgrad"):
-        from grouped_gemm_opt import _C, grouped_gemm_opt_fp8, quantize_fp8
+    elif args.profile in ("fp8", "mxfp8", "dgrad", "wgrad"):
+        from grouped_gemm_opt import (_C, grouped_gemm_opt_fp8, grouped_gemm_opt_mxfp8,
+                                      quantize_fp8, quantize_mxfp8)
         g = torch.Generator(device="cuda").manual_seed(0)
         x = torch.randn(T_TOK, K, device="cuda", generator=g).to(torch.bfloat16)
         w = (torch.randn(E, N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
@@ -329,6 +331,10 @@ def profile_run(args):
             xq, xs = quantize_fp8(x)
             wq, ws = quantize_fp8(w)
             fn = lambda: grouped_gemm_opt_fp8(xq, xs, wq, ws, tpe)  # noqa: E731
+        elif args.profile == "mxfp8":
+            xq, xs = quantize_mxfp8(x, tpe)
+            wq, ws = quantize_mxfp8(w)
+            fn = lambda: grouped_gemm_opt_mxfp8(xq, xs, wq, ws, tpe)  # noqa: E731
         else:
             dy = torch.randn(T_TOK, N, device="cuda", generator=g).to(torch.bfloat16)
             fn = (lambda: _C.grouped_gemm_dgrad(dy, w, tpe, 4, True)) if args.profile == "dgrad" \
@@ -430,6 +436,17 @@ def config_sweep(steps=60, warmup=5):
     total, _ = _timed(fn, steps, 1)
     ms = total / steps
     res["cfg2_fp8"] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
+    del xq, wq
+    # MXFP8 (e4m3 with UE8M0 scales per 32 K elements, applied by the tensor cores)
+    from grouped_gemm_opt import grouped_gemm_opt_mxfp8, quantize_mxfp8
+    xq, xs = quantize_mxfp8(x, td)
+    wq, ws = quantize_mxfp8(w)
+    fn = lambda: grouped_gemm_opt_mxfp8(xq, xs, wq, ws, td)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    total, _ = _timed(fn, steps, 1)
+    ms = total / steps
+    res["cfg2_mxfp8"] = {"ms": ms, "tflops": FLOP_PER_STEP / ms / 1e9}
     del x, dy, w, xq, wq
     torch.cuda.empty_cache()
     # Mixtral layer with FP8 (e4m3) grouped GEMMs on one GPU (the bf16 one is `moe_layer`)
@@ -450,6 +467,22 @@ def config_sweep(steps=60, warmup=5):
     ms = total / st
     res["mixtral_layer_fp8"] = {"ms": ms, "tokens_per_s": T2 / ms * 1e3,
                                 "tflops": 6.0 * T2 * k2 * H2 * F2 / ms / 1e9}
+    del qw
+    torch.cuda.empty_cache()
+    # the same layer with MXFP8 grouped GEMMs
+    from grouped_gemm_opt import fused_moe_mxfp8, quantize_moe_weights_mxfp8
+    g = torch.Generator(device="cuda").manual_seed(2)
+    qw = quantize_moe_weights_mxfp8(
+        (torch.randn(E2, 2 * F2, H2, device="cuda", generator=g) * 0.02).to(torch.bfloat16),
+        (torch.randn(E2, H2, F2, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+    torch.cuda.empty_cache()
+    fn = lambda: fused_moe_mxfp8(x, logits, qw, k2)  # noqa: E731
+    for _ in range(warmup):
+        fn()
+    total, _ = _timed(fn, st, 1)
+    ms = total / st
+    res["mixtral_layer_mxfp8"] = {"ms": ms, "tokens_per_s": T2 / ms * 1e3,
+                                  "tflops": 6.0 * T2 * k2 * H2 * F2 / ms / 1e9}
     del x, qw
     torch.cuda.empty_cache()
     # DeepSeek-V3-shaped layer on one GPU (all 256 experts local): decode and prefill token counts
@@ -484,7 +517,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the secondary-config sweep")
-    ap.add_argument("--profile", choices=["gemm", "moe", "fp8", "dgrad", "wgrad"], default=None,
+    ap.add_argument("--profile", choices=["gemm", "moe", "fp8", "mxfp8", "dgrad", "wgrad"], default=None,
                     help="minimal run for ncu captures: warm-up + steps of one path, no JSON")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

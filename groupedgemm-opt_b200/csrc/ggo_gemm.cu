@@ -303,9 +303,10 @@ struct GemmExtras {
   const void* b_sf = nullptr;
 };
 
-// MX tiles: CTA pairs of 256 x 192 (192 columns leave TMEM room for the scales next to two
-// accumulators). SwiGLU weights for the MX path are blocked by kMxGluBlock output columns:
-// [E, 2 * F_pad, K], F_pad = F rounded up to kMxGluBlock, block j = gate rows j*96.. then up rows.
+// MX tiles: CTA pairs of 256 x 192 (the rest of each accumulator's 256 TMEM columns holds the
+// scales). SwiGLU weights for the MX path are blocked by kMxGluBlock output columns:
+// [E, 2 * F_pad, K], F_pad = F rounded up to kMxGluBlock, block j = gate rows j*96.. then the
+// matching up rows.
 constexpr int kMxPairBN = 192;
 constexpr int kMxGluBlock = kMxPairBN / 2;
 int64_t mx_glu_rows(int64_t f) { return 2 * ((f + kMxGluBlock - 1) / kMxGluBlock) * kMxGluBlock; }

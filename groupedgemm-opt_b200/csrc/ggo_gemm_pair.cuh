@@ -25,8 +25,10 @@ struct PairLayout {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 A rows
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of the BN-row B tile
   // MX: this CTA's A scales (one 512-B atom: 128 rows x 4 K groups of 32) and the scales of the
-  // 256 weight rows around the tile (two atoms), behind the B half
-  static constexpr int kSfBytes = MX ? 3 * 512 : 0;
+  // weight rows from the 128-row block where the tile's B rows start (kSfbAtoms atoms: a tile
+  // width that is a multiple of 64 starts 0 or 64 rows into a block), behind the B half
+  static constexpr int kSfbAtoms = (64 + BN + 127) / 128;
+  static constexpr int kSfBytes = MX ? (1 + kSfbAtoms) * 512 : 0;
   static constexpr int kTxBytes = kABytes + kBBytes + kSfBytes;  // one CTA's loads per stage
   static constexpr int kStageBytes = (kTxBytes + 1023) / 1024 * 1024;  // 1024-B aligned stages
   static constexpr int kStagingBytes = 4 * 4096;  // TMA-store staging, 4 KB per epilogue warp
@@ -52,10 +54,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                              const __grid_constant__ CUtensorMap tmSFA,
                              const __grid_constant__ CUtensorMap tmSFB, const GemmParams p) {
   using L = PairLayout<BN, MX>;
-  // MX: the scales sit in TMEM columns 448-459, beside the two accumulators (0 and 256, each at
-  // most 192 wide); a 192-row B tile starts 0 or 64 rows into its first 128-row scale block
+  // MX: the scales of consecutive K steps rotate through 16-column TMEM slots (A: 4 columns, B:
+  // 4 per atom) in the gaps beside the two accumulators (columns BN..255 and 256+BN..511), so
+  // copying one step's scales never waits for the MMAs still reading the previous step's.
+  // Widths are multiples of 64, so B's scales start at an even column of the slot (0 or 2), the
+  // offsets the block-scaled MMA is used with here; a 224-wide variant (odd offsets, N = 224)
+  // stopped with a misaligned-address error and is not built.
   static_assert(!MX || (FP8 && !BMN && BN <= 192 && BN % 64 == 0), "MX tile");
-  constexpr uint32_t kSfaCol = 448, kSfbCol = 452;
+  static_assert(!MX || 4 + 4 * L::kSfbAtoms <= 16, "scale slot width");
+  constexpr uint32_t kSfSlotsPerGap = (256 - BN) / 16;
+  constexpr uint32_t kSfSlots = 2 * kSfSlotsPerGap;
+  static_assert(!MX || kSfSlots >= 2, "scale slots");
   constexpr int S = L::kStages;
   // BN = N of the pair tile = columns of each CTA's accumulator (multiple of 32, <= 256)
   static_assert(BN % 32 == 0 && BN <= 256 && (EPI == kEpiStore || BN % 64 == 0), "tile width");
@@ -214,8 +223,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               // scales from each CTA's own TMEM)
               const int w_row = epi_glu(EPI) ? 2 * info.n0 : info.n0;  // within the expert
               const int blk_b = (seg % p.num_experts) * ((p.n_b + 127) / 128) + w_row / 128;
-              tma_load_2d_pair(sf_dst + 512, &tmSFB, fb, 0, 2 * (blk_b * num_kb + kb));
-              tma_load_2d_pair(sf_dst + 1024, &tmSFB, fb, 0, 2 * ((blk_b + 1) * num_kb + kb));
+#pragma unroll
+              for (int i = 0; i < L::kSfbAtoms; ++i)
+                tma_load_2d_pair(sf_dst + 512 * (i + 1), &tmSFB, fb, 0,
+                                 2 * ((blk_b + i) * num_kb + kb));
             }
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -233,6 +244,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_f16(kTileM, BN, FP8 ? false : BF16, BMN);
       static_assert(!BMN || (BN / 2) % 64 == 0, "MN-major B halves are whole 64-column boxes");
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
+      uint32_t sf_slot = 0;  // MX: scale slot of the next K step
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
         if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
@@ -260,9 +272,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // scales of this stage into TMEM (in order with the MMAs below and the previous
             // stage's): A's 128 rows, then B's 256 rows as two 4-column atoms
             const uint32_t sf_addr = a_addr + L::kABytes + L::kBBytes;
+            const uint32_t kSfaCol = sf_slot < kSfSlotsPerGap
+                                         ? BN + 16u * sf_slot
+                                         : 256u + BN + 16u * (sf_slot - kSfSlotsPerGap);
+            const uint32_t kSfbCol = kSfaCol + 4;
+            if (++sf_slot == kSfSlots) sf_slot = 0;
             tmem_cp_32x128b_x4_pair(tmem_base + kSfaCol, sdesc_rows16(sf_addr));
-            tmem_cp_32x128b_x4_pair(tmem_base + kSfbCol, sdesc_rows16(sf_addr + 512));
-            tmem_cp_32x128b_x4_pair(tmem_base + kSfbCol + 4, sdesc_rows16(sf_addr + 1024));
+#pragma unroll
+            for (int i = 0; i < L::kSfbAtoms; ++i)
+              tmem_cp_32x128b_x4_pair(tmem_base + kSfbCol + 4 * i,
+                                      sdesc_rows16(sf_addr + 512 * (i + 1)));
             // weight row w of the tile has its scales in column (first row % 128 + w) / 32
             const uint32_t sfb_col =
                 kSfbCol + static_cast<uint32_t>(((epi_glu(EPI) ? 2 * n0 : n0) & 127) >> 5);

@@ -143,3 +143,4 @@ def test_mxfp8_large_k_many_tiles():
     xd = _deq(xq, xs, counts, K)
     wd = _deq(wq, ws, [N] * len(counts), K).view(len(counts), N, K)
     assert_parity(out, oracle.sequential_gemm(xd, wd, tpe), "mxfp8 large")
+
