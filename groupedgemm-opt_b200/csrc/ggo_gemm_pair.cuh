@@ -268,9 +268,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = BMN ? sdesc_sw128_mnmajor(a_addr + L::kABytes, 8192)
                                      : sdesc_sw128_kmajor(a_addr + L::kABytes);
           constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
-          if (MX) {
+          if constexpr (MX) {
             // scales of this stage into TMEM (in order with the MMAs below and the previous
-            // stage's): A's 128 rows, then B's 256 rows as two 4-column atoms
+            // stage's): A's 128 rows, then B's rows as kSfbAtoms 4-column atoms
             const uint32_t sf_addr = a_addr + L::kABytes + L::kBBytes;
             const uint32_t kSfaCol = sf_slot < kSfSlotsPerGap
                                          ? BN + 16u * sf_slot
