@@ -389,8 +389,11 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
     sc.a_atoms = mx_scale_atoms(rows, num_segments, k);
     sc.b = ex->b_sf;
     sc.b_atoms = static_cast<int64_t>(num_experts) * ((n_b + 127) / 128) * (k / 128);
-    // the kernel addresses scale atoms by 32-bit TMA row coordinates (two rows per atom)
-    if (2 * (sc.a_atoms + 4) > INT32_MAX || 2 * (sc.b_atoms + 4) > INT32_MAX)
+    // The kernel addresses scale atoms by 32-bit TMA row coordinates, two rows per atom. The
+    // largest coordinate it forms is 2 * (block * (k / 128) + kb) with block at most one past the
+    // last block (rank 1's half of a pair tile, the B tile's second block): bound that.
+    const int64_t kgroups = k / 128;
+    if (2 * (sc.a_atoms + kgroups) > INT32_MAX || 2 * (sc.b_atoms + kgroups) > INT32_MAX)
       return GGO_ERR_SHAPE;
     p.group_m = raster_group_m(k / 2, 256);
     p.glu_blocked = swiglu ? 1 : 0;

@@ -170,8 +170,11 @@ def grouped_gemm_opt_fp8(
 
 
 def quantize_mxfp8(x: torch.Tensor, tokens_per_expert: torch.Tensor = None):
-    """MX (OCP microscaling) e4m3 quantisation on the GPU: every 32 consecutive elements of a row
-    share one UE8M0 scale 2^(byte - 127). Returns (q float8_e4m3fn, scales uint8) with the scales
+    """MX e4m3 quantisation on the GPU in the OCP microscaling layout: every 32 consecutive
+    elements of a row share one UE8M0 scale 2^(byte - 127). The scale rule is non-saturating
+    (X = floor(log2 amax) - 8, plus one when the mantissa of amax exceeds 1.75, so no element
+    clips); the OCP MX v1.0 rule (floor(log2 amax) - 8 and clamping) can give a scale one lower.
+    Returns (q float8_e4m3fn, scales uint8) with the scales
     in the 128x4 blocked layout the block-scaled tensor cores read, each expert's rows starting a
     fresh 128-row block. Activations [T, K]: pass ``tokens_per_expert`` (the rows are
     expert-sorted). Weights [E, N, K]: leave it None (E segments of N rows). K % 128 == 0."""
@@ -195,7 +198,8 @@ def grouped_gemm_opt_mxfp8(
     """MXFP8 grouped GEMM: ``out[i] = sum_k (q_in[i,k] 2^s_in[i,k//32]) (q_w[e,n,k] 2^s_w[e,n,k//32])``
     in bf16, the block scales applied by the tensor cores (tcgen05 kind::mxf8f6f4.block_scale,
     fp32 accumulation). Operands and scales come from :func:`quantize_mxfp8` (the input quantised
-    with the same ``tokens_per_expert``)."""
+    with the same ``tokens_per_expert``). Always runs 256 x 192 CTA-pair tiles: there is no tile
+    configuration for the MX path."""
     assert input_q.is_cuda and weights_q.is_cuda
     tokens_per_expert = tokens_per_expert.to(torch.int64).contiguous()
     if not tokens_per_expert.is_cuda:

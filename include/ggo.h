@@ -157,9 +157,13 @@ int ggo_grouped_gemm_swiglu_fp8(const void* x_dev, const float* x_scale_dev,
 int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dtype, void* q_dev,
                           float* scale_dev, cudaStream_t stream);
 
-/* MXFP8: block-scaled e4m3 (OCP MX; no reference counterpart). Every 32 consecutive K elements
- * of a row share one UE8M0 scale 2^(byte - 127); the tensor cores apply both operands' scales
- * (tcgen05 kind::mxf8f6f4.block_scale) and accumulate in fp32.
+/* MXFP8: block-scaled e4m3 in the OCP MX layout (no reference counterpart). Every 32 consecutive
+ * K elements of a row share one UE8M0 scale 2^(byte - 127); the tensor cores apply both operands'
+ * scales (tcgen05 kind::mxf8f6f4.block_scale) and accumulate in fp32. The GEMMs accept any UE8M0
+ * scales; ggo_quantize_mxfp8 picks them with a non-saturating rule (below) that differs from the
+ * OCP MX v1.0 reference rule (floor(log2 amax) - emax, then clamping), so its scale bytes can
+ * differ from other MX producers' by one. The MXFP8 GEMMs always run 256 x 192 CTA-pair tiles:
+ * they take no tile configuration, and the Python wrappers ignore a tile_config argument. */
  * Scale layout ("128x4 blocked"): the rows of each segment start a fresh 128-row block after the
  * blocks of the previous segments; block b and K group g (128 elements, 4 scales) form the 512-B
  * atom at byte (b * K/128 + g) * 512, inside which row r (0..127) and scale j (0..3) of the group
