@@ -269,11 +269,21 @@ template <typename T16>
 __global__ void __launch_bounds__(256)
     combine_kernel(const T16* __restrict__ ys, const float* __restrict__ w,
                    const int32_t* __restrict__ slot_pos, int T, int H, int K,
-                   T16* __restrict__ out) {
+                   T16* __restrict__ out, const int* __restrict__ err) {
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
   const int vec = H / 8;
+  if (err != nullptr && *reinterpret_cast<const volatile int*>(err) != 0) {
+    // the data this token's rows came from is incomplete: hand back NaN, never stale numbers
+    uint4 nan4;
+    T16* nh = reinterpret_cast<T16*>(&nan4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) nh[i] = static_cast<T16>(__int_as_float(0x7fc00000));
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H);
+    for (int c = lane; c < vec; c += 32) dst[c] = nan4;
+    return;
+  }
   int ps[kMaxTopK];
   float wt[kMaxTopK];
   for (int j = 0; j < K; ++j) {
@@ -479,7 +489,9 @@ __global__ void ep_signal_kernel(PeerBoards pb, int world, int rank, int E, int 
 // incomplete and the host reports the error).
 __global__ void ep_wait_kernel(const int64_t* __restrict__ own_board, int world, int E, int slot,
                                long long epoch, int* err, long long limit) {
-  if (threadIdx.x < world) {
+  // an earlier phase already failed: this layer's data is void, do not wait out another limit
+  const bool failed = *reinterpret_cast<const volatile int*>(err) != 0;
+  if (threadIdx.x < world && !failed) {
     const volatile long long* f = reinterpret_cast<const volatile long long*>(
         own_board + static_cast<size_t>(kMaxPeers) * E + slot * kMaxPeers + threadIdx.x);
     const long long t0 = clock64();
@@ -700,6 +712,16 @@ int ggo_ep_wait(const int64_t* own_board, int world_size, int num_experts, int s
 int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
                     const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden, int top_k,
                     void* out_dev, int dtype, cudaStream_t stream) {
+  return ggo_moe_combine_checked(y_sorted_dev, topk_weights_dev, slot_pos_dev, num_tokens, hidden,
+                                 top_k, out_dev, dtype, nullptr, stream);
+}
+
+int ggo_moe_combine_checked(const void* y_sorted_dev, const float* topk_weights_dev,
+                            const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden,
+                            int top_k, void* out_dev, int dtype, const void* workspace_dev,
+                            cudaStream_t stream) {
+  // GgoWorkspace::error is the third int of the workspace
+  const int* err = workspace_dev ? static_cast<const int*>(workspace_dev) + 2 : nullptr;
   if (!y_sorted_dev || !topk_weights_dev || !slot_pos_dev || !out_dev) return GGO_ERR_INVALID_ARG;
   if (num_tokens < 0 || hidden <= 0 || top_k <= 0 || top_k > ggo::kMaxTopK)
     return GGO_ERR_INVALID_ARG;
@@ -713,11 +735,11 @@ int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
   if (dtype == GGO_DTYPE_BF16) {
     ggo::combine_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(y_sorted_dev), topk_weights_dev, slot_pos_dev, T,
-        static_cast<int>(hidden), top_k, static_cast<__nv_bfloat16*>(out_dev));
+        static_cast<int>(hidden), top_k, static_cast<__nv_bfloat16*>(out_dev), err);
   } else {
     ggo::combine_kernel<__half><<<grid, 256, 0, stream>>>(
         static_cast<const __half*>(y_sorted_dev), topk_weights_dev, slot_pos_dev, T,
-        static_cast<int>(hidden), top_k, static_cast<__half*>(out_dev));
+        static_cast<int>(hidden), top_k, static_cast<__half*>(out_dev), err);
   }
   return ggo::check_launch();
 }

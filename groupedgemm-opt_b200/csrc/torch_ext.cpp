@@ -374,7 +374,7 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> moe_permute(
 }
 
 torch::Tensor moe_combine(const torch::Tensor& y_sorted, const torch::Tensor& topk_weights,
-                          const torch::Tensor& slot_pos) {
+                          const torch::Tensor& slot_pos, bool checked) {
   TORCH_CHECK(y_sorted.is_cuda() && y_sorted.dim() == 2 && y_sorted.is_contiguous(),
               "y_sorted must be 2D contiguous CUDA");
   TORCH_CHECK(topk_weights.scalar_type() == torch::kFloat32 && topk_weights.is_contiguous(),
@@ -385,9 +385,11 @@ torch::Tensor moe_combine(const torch::Tensor& y_sorted, const torch::Tensor& to
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const int64_t T = topk_weights.size(0), k = topk_weights.size(1), H = y_sorted.size(1);
   auto out = torch::empty({T, H}, y_sorted.options());
-  const int st = ggo_moe_combine(y_sorted.data_ptr(), topk_weights.data_ptr<float>(),
-                                 slot_pos.data_ptr<int32_t>(), T, H, static_cast<int>(k),
-                                 out.data_ptr(), dtype_code(y_sorted), stream);
+  // checked: NaN output when the stream's workspace error word is set (an expired peer wait)
+  const int st = ggo_moe_combine_checked(
+      y_sorted.data_ptr(), topk_weights.data_ptr<float>(), slot_pos.data_ptr<int32_t>(), T, H,
+      static_cast<int>(k), out.data_ptr(), dtype_code(y_sorted),
+      checked ? workspace_for(y_sorted.device(), stream) : nullptr, stream);
   check_status(st, "MoE combine");
   return out;
 }
@@ -677,7 +679,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute, py::arg("hidden"), py::arg("topk_ids"), py::arg("scratch"),
         py::arg("num_experts"));
   m.def("moe_combine", &moe_combine, py::arg("y_sorted"), py::arg("topk_weights"),
-        py::arg("slot_pos"));
+        py::arg("slot_pos"), py::arg("checked") = false);
   m.def("workspace_error", &workspace_error, py::arg("device") = 0);
   m.def("abi_version", []() { return ggo_version(); });
   m.def("kernel_launches", []() { return static_cast<int64_t>(ggo_kernel_launches()); });

@@ -8,12 +8,13 @@ from grouped_gemm_opt.ops import (TileConfig, check_device_errors, grouped_gemm_
                                   quantize_mxfp8)
 from grouped_gemm_opt.triton_fused_moe import triton_fused_moe
 from grouped_gemm_opt.triton_grouped_gemm import triton_grouped_gemm
-from grouped_gemm_opt.moe import (EPBuffers, MoEFP8Weights, MoEMXFP8Weights, fused_moe,
-                                  fused_moe_fp8, fused_moe_mxfp8, quantize_moe_weights,
-                                  quantize_moe_weights_mxfp8)
+from grouped_gemm_opt.moe import (EPBuffers, MoEFP8Weights, MoEMXFP8Weights, StageEvents,
+                                  fused_moe, fused_moe_fp8, fused_moe_host, fused_moe_mxfp8,
+                                  quantize_moe_weights, quantize_moe_weights_mxfp8)
 
 __all__ = ["grouped_gemm_opt", "TileConfig", "triton_fused_moe", "triton_grouped_gemm",
            "fused_moe", "check_device_errors", "grouped_gemm_opt_host", "EPBuffers",
            "grouped_gemm_opt_fp8", "quantize_fp8", "fused_moe_fp8", "quantize_moe_weights",
            "MoEFP8Weights", "quantize_mxfp8", "grouped_gemm_opt_mxfp8", "mxfp8_block_gate_up",
-           "fused_moe_mxfp8", "quantize_moe_weights_mxfp8", "MoEMXFP8Weights"]
+           "fused_moe_mxfp8", "quantize_moe_weights_mxfp8", "MoEMXFP8Weights",
+           "fused_moe_host", "StageEvents"]

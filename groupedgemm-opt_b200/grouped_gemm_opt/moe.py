@@ -46,6 +46,41 @@ class MoEOps:
     combine: Callable    # (y_sorted, w, slot_pos) -> out [T, H]
 
 
+class StageEvents:
+    """Per-stage device timing of the layer: pass as ``fused_moe(..., timer=StageEvents())``.
+    Every stage boundary records a CUDA event on the current stream (no synchronisation), so the
+    layer runs exactly as it does without a timer. ``ms()`` (after a synchronize) returns the
+    summed milliseconds of every stage over all layers timed with this object."""
+
+    def __init__(self):
+        self._marks = []  # [(layer index, stage name, event)]
+        self._layer = -1
+
+    def start(self):
+        self._layer += 1
+        self.mark("start")
+
+    def mark(self, name: str):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self._marks.append((self._layer, name, ev))
+
+    def layers(self) -> int:
+        return self._layer + 1
+
+    def ms(self) -> dict:
+        tot = {}
+        for (l0, _, e0), (l1, name, e1) in zip(self._marks, self._marks[1:]):
+            if l0 == l1:
+                tot[name] = tot.get(name, 0.0) + e0.elapsed_time(e1)
+        return tot
+
+
+def _mark(timer, name):
+    if timer is not None:
+        timer.mark(name)
+
+
 def cuda_ops() -> MoEOps:
     from grouped_gemm_opt._native import _C
 
@@ -127,6 +162,13 @@ class EPBuffers:
         kernels (and their peer stores) are complete when it returns on any rank's stream."""
         dist.all_reduce(self.flag, group=self.group)
 
+    def check(self):
+        """Synchronises and raises RuntimeError if a peer wait of a layer on this stream expired
+        (a rank fell behind or left). Layers after such a failure return NaN rows rather than
+        stale data, so a caller that skips this check still cannot mistake them for results."""
+        from grouped_gemm_opt.ops import check_device_errors
+        check_device_errors(self.device.index)
+
     def close(self):
         if self._C is None:
             return
@@ -141,7 +183,7 @@ class EPBuffers:
 
 
 def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuffers",
-                   sort_by_m):
+                   sort_by_m, timer=None):
     """Expert-parallel layer over NVLink peer memory: the dispatch kernel writes rows into the
     owners' receive buffers, the down GEMM's epilogue writes results back into the sources'
     return buffers. The phases are ordered by device-side epoch flags in the IPC-shared sync
@@ -158,24 +200,34 @@ def _fused_moe_p2p(hidden, router_logits, w_gate_up, w_down, top_k, bufs: "EPBuf
     ep, dev, boards, own = bufs.epoch, hidden.device.index, bufs.ptrs["board"], bufs._own["board"]
     lim = bufs.wait_limit_cycles
     ids, w, tpe, scratch = C.moe_route(router_logits, top_k)
+    _mark(timer, "route")
     # phase 0: every rank's counts land in every board
     C.ep_publish_counts(tpe, boards, rank, 0, ep)
     C.ep_wait(own, world, E, 0, ep, lim, dev)
+    _mark(timer, "count_exchange")
     counts_all = bufs.board_counts[:world]
     slot_pos = C.ep_dispatch(hidden, ids, scratch, counts_all, rank, bufs.ptrs["recv"],
                              bufs.ptrs["origin"])
+    _mark(timer, "dispatch")
     # phase 1: every source has delivered its rows to this rank
     C.ep_signal(boards, rank, E, 1, ep, dev)
     C.ep_wait(own, world, E, 1, ep, lim, dev)
+    _mark(timer, "dispatch_wait")
     # receive buffer is expert-major: one segment per local expert, rows from every source
     seg_counts = counts_all[:, rank * el:(rank + 1) * el].sum(0)
     h = C.ep_grouped_gemm(bufs.recv, w_gate_up, seg_counts, el, True, None, [], sort_by_m)
+    _mark(timer, "gate_up")
     C.ep_grouped_gemm(h, w_down, seg_counts, el, False, bufs.origin, bufs.ptrs["back"],
                       sort_by_m)
+    _mark(timer, "down")
     # phase 2: every owner has scattered this rank's results back
     C.ep_signal(boards, rank, E, 2, ep, dev)
     C.ep_wait(own, world, E, 2, ep, lim, dev)
-    return C.moe_combine(bufs.back[:T * top_k], w, slot_pos)
+    _mark(timer, "return_wait")
+    # checked combine: if any wait above expired, the result is NaN instead of stale rows
+    out = C.moe_combine(bufs.back[:T * top_k], w, slot_pos, True)
+    _mark(timer, "combine")
+    return out
 
 
 def _check(hidden, router_logits, w_gate_up, w_down, top_k, world):
@@ -205,6 +257,7 @@ def fused_moe(
     sort_by_m: bool = True,
     ops: Optional[MoEOps] = None,
     ep_buffers: Optional[EPBuffers] = None,
+    timer: Optional[StageEvents] = None,
 ) -> torch.Tensor:
     """MoE layer forward.
 
@@ -219,38 +272,116 @@ def fused_moe(
         ops: compute stages (defaults to the CUDA kernels).
         ep_buffers: EPBuffers of `ep_group`: selects the fused peer-memory path (dispatch and
             result scatter over NVLink inside the kernels) instead of NCCL all-to-alls.
+        timer: a StageEvents that records a CUDA event after every stage (device timing).
 
     Returns: [T, H] = sum_j w[t,j] * down(silu(gate(x_t)) * up(x_t)) for the top-k experts.
     """
     world = dist.get_world_size(ep_group) if ep_group is not None else 1
     T, H, E, el = _check(hidden, router_logits, w_gate_up, w_down, top_k, world)
+    if timer is not None:
+        timer.start()
     if ep_buffers is not None and world > 1 and ops is None:
         return _fused_moe_p2p(hidden.contiguous(), router_logits, w_gate_up, w_down, top_k,
-                              ep_buffers, sort_by_m)
+                              ep_buffers, sort_by_m, timer)
     if ops is None:
         ops = cuda_ops()
     hidden = hidden.contiguous()
     ids, w, tpe, scratch = ops.route(router_logits, top_k)
+    _mark(timer, "route")
     xs, _sorted_token, slot_pos = ops.permute(hidden, ids, scratch, E)
+    _mark(timer, "dispatch")
     if world == 1:
         h = ops.gate_up(xs, w_gate_up, tpe, E, sort_by_m)
+        _mark(timer, "gate_up")
         y = ops.down(h, w_down, tpe, E, sort_by_m)
-        return ops.combine(y, w, slot_pos)
+        _mark(timer, "down")
+        out = ops.combine(y, w, slot_pos)
+        _mark(timer, "combine")
+        return out
 
     send_counts = tpe.view(world, el)
     recv_counts = torch.empty_like(tpe)
     dist.all_to_all_single(recv_counts, tpe, group=ep_group)
     # one host read of both split vectors
     splits = torch.stack([send_counts.sum(1), recv_counts.view(world, el).sum(1)]).cpu()
+    _mark(timer, "count_exchange")
     send_splits = splits[0].tolist()
     recv_splits = splits[1].tolist()
     x_recv = xs.new_empty((int(sum(recv_splits)), H))
     dist.all_to_all_single(x_recv, xs, recv_splits, send_splits, group=ep_group)
+    _mark(timer, "dispatch_all_to_all")
     h = ops.gate_up(x_recv, w_gate_up, recv_counts, el, sort_by_m)
+    _mark(timer, "gate_up")
     y = ops.down(h, w_down, recv_counts, el, sort_by_m)
+    _mark(timer, "down")
     y_back = y.new_empty((xs.size(0), H))
     dist.all_to_all_single(y_back, y, send_splits, recv_splits, group=ep_group)
-    return ops.combine(y_back, w, slot_pos)
+    _mark(timer, "return_all_to_all")
+    out = ops.combine(y_back, w, slot_pos)
+    _mark(timer, "combine")
+    return out
+
+
+def fused_moe_host(
+    hidden: torch.Tensor,
+    router_logits: torch.Tensor,
+    w_gate_up: torch.Tensor,
+    w_down: torch.Tensor,
+    top_k: int,
+    out: Optional[torch.Tensor] = None,
+    chunks: int = 4,
+    ep_group: Optional[dist.ProcessGroup] = None,
+    ep_buffers: Optional[EPBuffers] = None,
+    sort_by_m: bool = True,
+) -> torch.Tensor:
+    """:func:`fused_moe` on HOST-resident tokens: ``hidden`` [T, H] and ``router_logits`` [T, E]
+    in (pinned) host memory, weights on the GPU, result into ``out`` [T, H] in host memory
+    (allocated pinned if not given).
+
+    The tokens are split into ``chunks`` consecutive groups. Group i+1 is copied in on a copy
+    stream while the layer runs on group i on the current stream, and group i-1's result is
+    copied out on a third stream, so PCIe traffic hides behind the layer. Every rank of an
+    expert-parallel group must call this with the same ``chunks`` (each chunk is one layer
+    call, a collective over the group). Returns ``out`` once the work is enqueued; it is
+    complete when the current stream is synchronised (all streams are joined back to it)."""
+    assert not hidden.is_cuda and not router_logits.is_cuda, "tokens must be in host memory"
+    assert w_gate_up.is_cuda and w_down.is_cuda
+    T, H = hidden.shape
+    dev = w_gate_up.device
+    if out is None:
+        out = torch.empty(T, H, dtype=hidden.dtype, pin_memory=True)
+    chunks = max(1, min(chunks, T)) if T > 0 else 1
+    bounds = [T * i // chunks for i in range(chunks + 1)]
+    main = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    xs, ls, copied = [], [], []
+    with torch.cuda.stream(s_in):
+        for i in range(chunks):
+            a, b = bounds[i], bounds[i + 1]
+            xs.append(hidden[a:b].to(dev, non_blocking=True))
+            ls.append(router_logits[a:b].to(dev, non_blocking=True))
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+            copied.append(ev)
+    for i in range(chunks):
+        a, b = bounds[i], bounds[i + 1]
+        main.wait_event(copied[i])
+        y = fused_moe(xs[i], ls[i], w_gate_up, w_down, top_k, ep_group=ep_group,
+                      sort_by_m=sort_by_m, ep_buffers=ep_buffers)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            out[a:b].copy_(y, non_blocking=True)
+            y.record_stream(s_out)
+        xs[i].record_stream(main)
+        ls[i].record_stream(main)
+    main.wait_stream(s_out)
+    main.wait_stream(s_in)
+    return out
 
 
 @dataclass

@@ -163,7 +163,7 @@ int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dty
  * scales; ggo_quantize_mxfp8 picks them with a non-saturating rule (below) that differs from the
  * OCP MX v1.0 reference rule (floor(log2 amax) - emax, then clamping), so its scale bytes can
  * differ from other MX producers' by one. The MXFP8 GEMMs always run 256 x 192 CTA-pair tiles:
- * they take no tile configuration, and the Python wrappers ignore a tile_config argument. */
+ * they take no tile configuration.
  * Scale layout ("128x4 blocked"): the rows of each segment start a fresh 128-row block after the
  * blocks of the previous segments; block b and K group g (128 elements, 4 scales) form the 512-B
  * atom at byte (b * K/128 + g) * 512, inside which row r (0..127) and scale j (0..3) of the group
@@ -247,6 +247,16 @@ int ggo_moe_combine(const void* y_sorted_dev, const float* topk_weights_dev,
                     const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden, int top_k,
                     void* out_dev, int dtype, cudaStream_t stream);
 
+/* ggo_moe_combine that refuses to hand back a result built from incomplete data: when the
+ * workspace error word (see ggo_workspace_error) is non-zero as the kernel runs -- e.g. an
+ * expert-parallel peer wait expired, so the receive/return buffers may hold a previous layer's
+ * rows -- every output element is written as NaN instead. No host synchronisation. No reference
+ * counterpart (the reference is single-device). */
+int ggo_moe_combine_checked(const void* y_sorted_dev, const float* topk_weights_dev,
+                            const int32_t* slot_pos_dev, int64_t num_tokens, int64_t hidden,
+                            int top_k, void* out_dev, int dtype, const void* workspace_dev,
+                            cudaStream_t stream);
+
 /* ----------------------------------------------------------------- expert parallelism
  * The fused expert-parallel path over NVLink peer memory. None of these has a counterpart in the
  * reference, which is single-device. Buffers are shared between the ranks of one node through
@@ -289,7 +299,9 @@ int ggo_ep_dispatch(const void* x_dev, int64_t num_tokens, int64_t hidden, int n
  *                          `stream`, which must end with a system-scope fence).
  *   ggo_ep_wait:           wait until every rank posted `epoch` for `slot` on this rank's board;
  *                          bounded by limit_cycles (SM clock), after which the workspace error
- *                          word records GGO_ERR_DEVICE_TIMEOUT (read it with ggo_workspace_error). */
+ *                          word records GGO_ERR_DEVICE_TIMEOUT (read it with ggo_workspace_error).
+ *                          A wait that finds the error word already set returns at once, so one
+ *                          expired wait does not make every later phase wait out its limit too. */
 size_t ggo_ep_board_bytes(int num_experts);
 int ggo_ep_publish_counts(const int64_t* tokens_per_expert_dev, int64_t* const* boards,
                           int world_size, int rank, int num_experts, int slot, int64_t epoch,

@@ -13,7 +13,7 @@ jeshxxx/GroupedGEMM-OPT):
   zipf_counts / dirichlet_counts   the seeded tpe generators of the BASELINE configs (cfg3), which
                            the reference does not ship (its random_distribution,
                            benchmark.py:72-79, is unseeded).
-  route / permute / combine / moe_layer   the fused-MoE layer. The reference has no router,
+  route / permute / combine / moe_layer / moe_tokens   the fused-MoE layer. The reference has no router,
                            permute or combine (its triton_fused_moe.py:81-101 gathers through an
                            identity map), so these restate the conventions documented in
                            grouped_gemm_opt/moe.py. Parity of these stages is UNPINNED (no
@@ -61,11 +61,12 @@ def sequential_gemm(input: torch.Tensor, weights: torch.Tensor,
 
 
 def segments_gemm(input: torch.Tensor, weights: torch.Tensor, seg_counts: torch.Tensor,
-                  num_experts: int) -> torch.Tensor:
-    """Segment form: segment s multiplies by expert s % num_experts (fp32 result)."""
-    x = input.float()
-    w = weights.float()
-    out = torch.zeros(x.size(0), w.size(1))
+                  num_experts: int, native: bool = False) -> torch.Tensor:
+    """Segment form: segment s multiplies by expert s % num_experts (fp32 result). ``native``:
+    F.linear in the operands' own dtype, as the reference's loop runs it (result in that dtype)."""
+    x = input if native else input.float()
+    w = weights if native else weights.float()
+    out = torch.zeros(x.size(0), w.size(1), dtype=x.dtype)
     off = 0
     for s, m in enumerate(seg_counts.tolist()):
         if m > 0:
@@ -75,11 +76,13 @@ def segments_gemm(input: torch.Tensor, weights: torch.Tensor, seg_counts: torch.
 
 
 def swiglu_gemm(x: torch.Tensor, w_gate_up: torch.Tensor, seg_counts: torch.Tensor,
-                num_experts: int) -> torch.Tensor:
-    """h = silu(x W_gate^T) * (x W_up^T) per segment; W_gu rows [0,F) gate, [F,2F) up. fp32."""
+                num_experts: int, native: bool = False) -> torch.Tensor:
+    """h = silu(x W_gate^T) * (x W_up^T) per segment; W_gu rows [0,F) gate, [F,2F) up. fp32
+    (``native``: the GEMM in the operands' dtype, the activation in fp32, h in that dtype)."""
     f = w_gate_up.size(1) // 2
-    gu = segments_gemm(x, w_gate_up, seg_counts, num_experts)
-    return F.silu(gu[:, :f]) * gu[:, f:]
+    gu = segments_gemm(x, w_gate_up, seg_counts, num_experts, native).float()
+    h = F.silu(gu[:, :f]) * gu[:, f:]
+    return h.to(x.dtype) if native else h
 
 
 # ----------------------------------------------------------------------------- distributions
@@ -155,22 +158,55 @@ def combine(y_sorted: torch.Tensor, w: np.ndarray, slot_pos: np.ndarray) -> torc
 
 
 def moe_layer(hidden: torch.Tensor, logits: torch.Tensor, w_gate_up: torch.Tensor,
-              w_down: torch.Tensor, top_k: int, round_to=None) -> torch.Tensor:
+              w_down: torch.Tensor, top_k: int, round_to=None, native: bool = False) -> torch.Tensor:
     """Whole layer in fp32. With ``round_to`` (e.g. torch.bfloat16) the intermediate activations
-    (gathered rows, h, y) are rounded to that dtype as the GPU pipeline stores them."""
+    (gathered rows, h, y) are rounded to that dtype as the GPU pipeline stores them. ``native``
+    runs the two grouped GEMMs as the reference's per-expert F.linear loop in the weights' own
+    dtype (benchmark.py:91-107), the form timed as the CPU baseline of the layer."""
     ids, w, tpe = route(logits.float().numpy(), top_k)
     E = logits.size(1)
-    _, slot_pos = permute_indices(ids, E)
-    sorted_token, _ = permute_indices(ids, E)
+    sorted_token, slot_pos = permute_indices(ids, E)
     xs = hidden[torch.from_numpy(sorted_token.astype(np.int64))]
     counts = torch.from_numpy(tpe)
-    h = swiglu_gemm(xs, w_gate_up, counts, E)
+    h = swiglu_gemm(xs, w_gate_up, counts, E, native)
     if round_to is not None:
         h = h.to(round_to)
-    y = segments_gemm(h, w_down, counts, E)
+    y = segments_gemm(h, w_down, counts, E, native)
     if round_to is not None:
         y = y.to(round_to)
     return combine(y, w, slot_pos)
+
+
+def moe_tokens(hidden: torch.Tensor, logits: torch.Tensor, expert_weights, top_k: int,
+               round_to=None) -> torch.Tensor:
+    """moe_layer for a SAMPLE of tokens whose experts' weights are fetched one at a time:
+    ``expert_weights(e)`` returns (w_gate_up[e] [2F, H], w_down[e] [H, F]) on the CPU. Tokens
+    are independent in the layer (routing, the GEMM rows and the combine are all per token), so
+    the rows for a sample equal the same rows of the whole layer. fp32, rounding as moe_layer."""
+    ids, w, _ = route(logits.float().numpy(), top_k)
+    T, k = ids.shape
+    x = hidden.float()
+    ys = {}
+    for e in np.unique(ids):
+        wgu, wd = expert_weights(int(e))
+        f = wgu.size(0) // 2
+        rows = np.argwhere(ids == e)  # (t, j) pairs in token order
+        xe = x[torch.from_numpy(rows[:, 0].astype(np.int64))]
+        gu = F.linear(xe, wgu.float())
+        h = F.silu(gu[:, :f]) * gu[:, f:]
+        if round_to is not None:
+            h = h.to(round_to).float()
+        y = F.linear(h, wd.float())
+        if round_to is not None:
+            y = y.to(round_to).float()
+        for i, (t, j) in enumerate(rows):
+            ys[(int(t), int(j))] = y[i]
+    out = torch.zeros(T, x.size(1))
+    wt = torch.from_numpy(np.asarray(w, dtype=np.float32))
+    for t in range(T):
+        for j in range(k):
+            out[t] += wt[t, j] * ys[(t, j)]
+    return out
 
 
 # ----------------------------------------------------------------------------- MXFP8

@@ -52,3 +52,29 @@ def test_ep_peer_wait_times_out_then_succeeds():
     torch.cuda.synchronize()
     ggo.check_device_errors(0)
     assert int(board[8 * E + 3 * 8 + 0]) == 1  # flags[slot 3][rank 0]
+
+
+def test_checked_combine_poisons_after_expired_wait():
+    """After an expired peer wait the checked combine (the last stage of the fused
+    expert-parallel layer) returns NaN rows instead of numbers built from stale buffers; once the
+    error is read and cleared it combines normally again."""
+    import grouped_gemm_opt as ggo
+    from grouped_gemm_opt import _C
+    E, T, H, k = 8, 16, 64, 2
+    g = torch.Generator().manual_seed(0)
+    y = torch.randn(T * k, H, generator=g).to(torch.bfloat16).to(DEV)
+    w = torch.rand(T, k, generator=g).to(DEV)
+    pos = torch.randperm(T * k, generator=g).to(torch.int32).to(DEV)
+    ggo.check_device_errors(0)
+    good = _C.moe_combine(y, w, pos, True)
+    assert torch.isfinite(good.float()).all()
+    board = torch.zeros(_C.ep_board_bytes(E) // 8, dtype=torch.int64, device=DEV)
+    _C.ep_wait(board.data_ptr(), 1, E, 2, 1, 1 << 24, 0)  # nobody posts: the wait expires
+    bad = _C.moe_combine(y, w, pos, True)
+    torch.cuda.synchronize()
+    assert torch.isnan(bad.float()).all()
+    assert torch.isfinite(_C.moe_combine(y, w, pos).float()).all()  # unchecked form unaffected
+    with pytest.raises(RuntimeError, match="error code"):
+        ggo.check_device_errors(0)
+    again = _C.moe_combine(y, w, pos, True)
+    assert torch.equal(again, good)

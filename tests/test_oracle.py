@@ -178,3 +178,22 @@ def test_mx_gate_up_blocking_round_trip():
     assert b.shape == (3, 2 * 288, 128)
     assert torch.equal(b[:, 96:192], w[:, 200:296])  # block 0: gate rows 0..95 then up rows 0..95
     assert torch.equal(oracle.mx_unblock_gate_up(b, 200), w)
+
+
+def test_moe_tokens_equals_layer_rows():
+    """The sample form of the layer oracle (used by the expert-parallel parity checks) gives the
+    same rows as the whole-layer oracle, and the native-dtype form stays within bf16 rounding."""
+    g = torch.Generator().manual_seed(4)
+    T, H, F, E, k = 96, 64, 48, 8, 3
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, generator=g)
+    wgu = (torch.randn(E, 2 * F, H, generator=g) * 0.1).to(torch.bfloat16)
+    wd = (torch.randn(E, H, F, generator=g) * 0.1).to(torch.bfloat16)
+    full = oracle.moe_layer(x, logits, wgu, wd, k, round_to=torch.bfloat16)
+    idx = torch.tensor([0, 5, 17, 40, 41, 95])
+    part = oracle.moe_tokens(x[idx], logits[idx], lambda e: (wgu[e], wd[e]), k,
+                             round_to=torch.bfloat16)
+    assert torch.allclose(part, full[idx], rtol=1e-5, atol=1e-6)
+    nat = oracle.moe_layer(x, logits, wgu, wd, k, native=True)
+    rel = ((nat - full).abs().max() / full.abs().max()).item()
+    assert rel < 2e-2, rel
