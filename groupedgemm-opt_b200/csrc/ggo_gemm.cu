@@ -141,14 +141,21 @@ int make_b_map(CUtensorMap* m, const void* b, int64_t b_rows, const GemmParams& 
 template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, int dev,
            cudaStream_t stream) {
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb, mc, mas;
+  memset(&mas, 0, sizeof(mas));
   GemmParams q = p;
   if (FP8) {
     if (int st = make_map_fp8(&ma, a, q.rows, q.k, kBM)) return st;
     if (int st = make_map_fp8(&mb, b, b_rows, q.k, 128)) return st;
+    q.skinny_max = 0;
   } else {
     if (int st = make_map(&ma, a, q.rows, q.k, BF16, kBM)) return st;
     if (int st = make_b_map<BMN>(&mb, b, b_rows, q, BF16, 128)) return st;
+    if (BMN) {
+      q.skinny_max = 0;
+    } else if (q.skinny_max > 0) {  // input boxes of kSkinnyRows rows for the skinny tiles
+      if (int st = make_map(&mas, a, q.rows, q.k, BF16, kSkinnyRows)) return st;
+    }
   }
   if (int st = make_out_map(&mc, &q, BF16)) return st;
   auto kern = grouped_gemm_kernel<BN, EPI, BF16, BMN, FP8>;
@@ -160,7 +167,7 @@ int launch(const void* a, const void* b, int64_t b_rows, const GemmParams& p, in
   const int64_t ub = ((p.rows + kBM - 1) / kBM + p.num_segments) * n_tiles;  // tile upper bound
   const int grid = static_cast<int>(ub < sms ? ub : sms);
   if (grid <= 0) return GGO_OK;
-  kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, q);
+  kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, mas, q);
   return check_launch();
 }
 
@@ -374,6 +381,12 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.split_tail_ntiles = 1;
   p.split_min_tiles = 0;
   p.glu_blocked = 0;
+  // GGO_SKINNY_ROWS: row limit of the swapped-operand tiles (default 64, 0 disables)
+  {
+    const char* e = getenv("GGO_SKINNY_ROWS");
+    const int v = e ? atoi(e) : kSkinnyRows;
+    p.skinny_max = v < 0 ? 0 : (v > kSkinnyRows ? kSkinnyRows : v);
+  }
   p.rows_is_bound = ex ? ex->rows_is_bound : 0;
   p.row_scale = fp8 ? ex->row_scale : nullptr;
   p.col_scale = fp8 ? ex->col_scale : nullptr;

@@ -99,8 +99,15 @@ struct GemmParams {
   // [n0, n0 + w) read weight rows [2 n0, 2 n0 + 2w): w gate rows then the w matching up rows,
   // w = the tile's output width (the layout the MX path's weight preparation writes)
   int glu_blocked;
+  // Skinny tiles: a tile of at most this many rows (a short segment, or a segment's last rows)
+  // runs with the operands swapped -- weight rows on the MMA's M side, the tile's rows on its N
+  // side rounded up to 16 -- so the tensor cores do work for the rows that exist instead of a
+  // 128-row block. 0 disables. Single-CTA kernel, bf16/fp16 K-major weights, plain or SwiGLU.
+  int skinny_max;
   GgoWorkspace* ws;
 };
+
+constexpr int kSkinnyRows = 64;  // rows of the input box a skinny tile loads (its row limit)
 
 struct TileInfo {
   int row0;    // first input row of the tile
@@ -109,7 +116,8 @@ struct TileInfo {
   int brow0;   // first W row of box 0 (and box 1 = brow1)
   int brow1;
   int seg;     // segment of the tile
-  int pad[2];
+  int skinny;  // 1: swapped-operand tile for a short row block (single-CTA kernel only)
+  int pad;
 };
 
 template <int BN>
@@ -491,16 +499,55 @@ __device__ __forceinline__ OutT* output_row(const GemmParams& p, const TileInfo&
          static_cast<size_t>(o & 0x0fffffff) * p.n_out;
 }
 
+// Epilogue of a skinny (swapped-operand) tile. The accumulator is transposed: TMEM lane = weight
+// row, column = the tile's input row. The warp holding lanes [32 ew, 32 ew + 32) of weight half h
+// (TMEM columns [128 h, 128 h + 64)) owns output columns n0 + 128 h + 32 ew + lane (plain), or
+// n0 + 32 ew + lane with gate in half 0 and up in half 1 (SwiGLU). For every input row of the
+// tile the 32 lanes store 32 consecutive output columns (64 contiguous bytes). All 32 lanes must
+// call it (tcgen05.ld is warp-collective).
+template <int BN, int EPI, bool BF16, typename OutT>
+__device__ __forceinline__ void store_skinny(uint32_t t_row, const GemmParams& p,
+                                             const TileInfo& info, int ew) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kHalves = epi_glu(EPI) ? 1 : BN / 128;
+#pragma unroll 1
+  for (int h = 0; h < kHalves; ++h) {
+    const int col = info.n0 + 128 * h + 32 * ew + lane;
+    const bool col_ok = col < p.n_out;
+#pragma unroll 1
+    for (int cb = 0; cb < info.rows; cb += 32) {
+      uint32_t v[32];
+      uint32_t u[32];
+      tmem_ld_32x32b_x32(t_row + 128 * h + cb, v);
+      if (epi_glu(EPI)) tmem_ld_32x32b_x32(t_row + 128 + cb, u);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int r = cb + j;
+        const bool ok = r < info.rows && info.row0 + r < p.rows;
+        float y = __uint_as_float(v[j]);
+        if (epi_glu(EPI)) y = y / (1.0f + __expf(-y)) * __uint_as_float(u[j]);
+        OutT* dst = output_row<OutT>(p, info, r, ok);
+        if (ok && col_ok) dst[col] = static_cast<OutT>(y);
+      }
+    }
+  }
+}
+
 template <int BN, int EPI, bool BF16, bool BMN = false, bool FP8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmC,
+                        const __grid_constant__ CUtensorMap tmAs, const GemmParams p) {
   using L = SmemLayout<BN>;
   constexpr int S = L::kStages;
   constexpr int kTmemCols = 2 * BN;             // two accumulators
   constexpr int kOutBN = epi_glu(EPI) ? BN / 2 : BN;
   constexpr bool kTmaStoreOk = kOutBN % 64 == 0;  // output boxes are 64 columns wide
+  // skinny tiles: tmAs is the input map with kSkinnyRows-row boxes
+  constexpr bool kSkinnyOk = !FP8 && !BMN && (EPI == kEpiStore || EPI == kEpiSwiGLU);
+  constexpr int kSkinnyABytes = kSkinnyRows * kBK * 2;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -574,6 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         info.rows = 0;
         if (t < total_tiles)
           info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+        info.skinny = (kSkinnyOk && info.rows > 0 && info.rows <= p.skinny_max) ? 1 : 0;
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer)) break;
         ring[q] = info;
         mbar_arrive(&schf_bar[q]);
@@ -590,8 +638,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!skip) {
             uint8_t* a_dst = tiles + stage * L::kStageBytes;
             uint8_t* b_dst = a_dst + L::kABytes;
-            mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kStageK, info.row0);
+            if (kSkinnyOk && info.skinny) {  // only the tile's first kSkinnyRows input rows
+              mbar_arrive_expect_tx(&full_bar[stage], kSkinnyABytes + L::kBBytes);
+              tma_load_2d(a_dst, &tmAs, &full_bar[stage], kb * kStageK, info.row0);
+            } else {
+              mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kStageK, info.row0);
+            }
             if (BMN) {  // BN/64 boxes of [64 reduction rows][64 output columns]
 #pragma unroll
               for (int i = 0; i < BN / 64; ++i)
@@ -622,6 +675,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (true) {
         if (!mbar_wait(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
         const bool valid = ring[q].rows > 0;
+        const bool skinny = kSkinnyOk && ring[q].skinny;
+        // skinny: M = 128 weight rows per MMA, N = the tile's rows rounded up to 16
+        const uint32_t idesc_s = idesc_f16(kBM, (ring[q].rows + 15) & ~15, BF16, false);
         mbar_arrive(&sche_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (!valid) break;
@@ -642,6 +698,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           // per 16-element K step: A (K-major) advances 32 B inside its swizzle atom; a K-major
           // B likewise, an MN-major B by 16 rows of 128 B (two 8-row atoms)
           constexpr uint64_t kBStep = BMN ? (2048 >> 4) : 2;
+          if (kSkinnyOk && skinny) {
+            // weights (the B slot, 128 rows per half) as the M-side operand, the tile's rows
+            // (the A slot) as the N side; half h accumulates into TMEM columns [128 h, ...)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+              for (int h = 0; h < BN / 128; ++h)
+                mma_f16_ss(d_tmem + 128 * h,
+                           sdesc_sw128_kmajor(a_addr + L::kABytes + h * 16384) + 2 * kk,
+                           adesc + 2 * kk, idesc_s, (kb | kk) != 0);
+            }
+            mma_commit(&empty_bar[stage]);
+            if (++stage == S) { stage = 0; phase ^= 1; }
+            continue;
+          }
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {  // four 32-byte K steps per 128-byte stage row
             if (FP8)
@@ -674,6 +745,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = r_local < info.rows && info.row0 + r_local < p.rows;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + acc * BN;
       using OutT = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      if (kSkinnyOk && info.skinny) {
+        store_skinny<BN, EPI, BF16, OutT>(t_row, p, info, ew);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce_bar[acc]);
+        if (++acc == 2) { acc = 0; aphase ^= 1; }
+        continue;
+      }
       OutT* out_row = output_row<OutT>(p, info, r_local, row_ok);
       const bool warp_tma = kTmaStoreOk && p.use_tma_store && ew * 32 + 32 <= info.rows;
       constexpr bool kScaled = EPI == kEpiScaled || EPI == kEpiScaledSwiGLU;

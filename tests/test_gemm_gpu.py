@@ -362,3 +362,49 @@ def test_backward_cfg2_full_size_sampled():
     cols = torch.randint(0, K, (16,), generator=torch.Generator().manual_seed(1))
     ref = dy[off:off + 554].float().cpu().T @ x[off:off + 554][:, cols.to(DEV)].float().cpu()
     assert_parity(dw[e][:, cols.to(DEV)], ref, "wgrad cfg2 expert 7")
+
+
+SKINNY_COUNTS = [1, 7, 8, 63, 64, 65, 16, 17, 0, 31, 32, 33, 128 + 5, 256 + 64]
+
+
+@pytest.mark.parametrize("tc", [0, 1, 4])
+@pytest.mark.parametrize("skinny", ["64", "0"])
+def test_skinny_segments(ggo, tc, skinny, monkeypatch):
+    """Short segments (and short last blocks of longer ones) run swapped-operand tiles: weight
+    rows on the MMA's M side, the segment's rows on its N side. Both that path and the 128-row
+    path (GGO_SKINNY_ROWS=0) must match the oracle, N not a multiple of the tile width."""
+    monkeypatch.setenv("GGO_SKINNY_ROWS", skinny)
+    x, w, tpe = gemm_inputs(SKINNY_COUNTS, 320, 640, seed=11)
+    ref = oracle.sequential_gemm(x, w, tpe)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV), tc)
+    assert_parity(out, ref, f"skinny={skinny} tc={tc}")
+    ggo.check_device_errors(0)
+
+
+@pytest.mark.parametrize("skinny", ["64", "0"])
+def test_skinny_swiglu_and_fp16(ggo, skinny, monkeypatch):
+    from grouped_gemm_opt import _C
+    monkeypatch.setenv("GGO_SKINNY_ROWS", skinny)
+    x, w, tpe = gemm_inputs(SKINNY_COUNTS, 256, 2 * 384, seed=12)
+    ref = oracle.swiglu_gemm(x, w, tpe, len(SKINNY_COUNTS))
+    h = _C.grouped_gemm_swiglu(x.to(DEV), w.to(DEV), tpe.to(DEV), len(SKINNY_COUNTS), True)
+    assert_parity(h, ref, f"skinny swiglu={skinny}")
+    x, w, tpe = gemm_inputs(SKINNY_COUNTS, 192, 520, seed=13, dtype=torch.float16)
+    out = ggo.grouped_gemm_opt(x.to(DEV), w.to(DEV), tpe.to(DEV))
+    assert out.dtype == torch.float16
+    assert_parity(out, oracle.sequential_gemm(x, w, tpe), f"skinny fp16={skinny}")
+
+
+def test_skinny_decode_shape(ggo):
+    """DSv3-decode-like grouped GEMM: 256 experts of about 8 rows, K=7168, N=4096."""
+    g = torch.Generator().manual_seed(14)
+    tpe = torch.bincount(torch.randint(0, 256, (2048,), generator=g), minlength=256)
+    x = torch.randn(2048, 7168, generator=g).to(torch.bfloat16)
+    wd = (torch.randn(256, 4096, 7168, device=DEV) * 0.02).to(torch.bfloat16)
+    out = ggo.grouped_gemm_opt(x.to(DEV), wd, tpe.to(DEV))
+    # check the rows of a few experts (each row depends only on its expert's weights)
+    off = torch.cat([torch.zeros(1, dtype=torch.int64), tpe.cumsum(0)])
+    for e in (0, 17, 100, 255):
+        a, b = int(off[e]), int(off[e + 1])
+        ref = torch.nn.functional.linear(x[a:b].float(), wd[e].float().cpu())
+        assert_parity(out[a:b], ref, f"decode expert {e}")
