@@ -370,7 +370,7 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.n_out = static_cast<int>(n);
   p.n_b = static_cast<int>(n_b);
   p.k = static_cast<int>(k);
-  p.sort_by_m = sort_by_m ? 1 : 0;
+  p.sort_by_m = sort_by_m ? env_int("GGO_SEG_ORDER", 2) : 0;
   p.group_m = raster_group_m(k, 128);  // re-derived below for 256-row pair tiles
   // Test hook for the bounded waits: GGO_TEST_INJECT_STALL=1 makes the first CTA leave one
   // pipeline stage unarmed and lowers the wait limit to 2^24 cycles (~10 ms). The kernel then

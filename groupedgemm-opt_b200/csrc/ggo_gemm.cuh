@@ -79,7 +79,7 @@ struct GemmParams {
   int n_out;              // columns of `out` (N, or F for SwiGLU)
   int n_b;                // rows of one expert's W (N, or 2F for SwiGLU)
   int k;                  // K
-  int sort_by_m;          // process segments heaviest-first
+  int sort_by_m;          // 0 segment order; 1 heaviest first; 2 heaviest/lightest interleaved
   int group_m;            // m-tiles per raster group (>= 1)
   void* out;              // [rows, n_out], bf16 or fp16
   int rows_is_bound;      // 1: `rows` is a capacity; counts may sum to less (no mismatch error)
@@ -243,8 +243,17 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
         __syncthreads();
       }
     }
-    for (int i = threadIdx.x; i < nseg; i += kThreads)
-      t_order[i] = static_cast<int>(keys[i] & 0xffffffffu);
+    if (p.sort_by_m == 2) {
+      // interleave heaviest and lightest: compute-bound blocks of long segments run beside the
+      // weight-streaming blocks of short ones, so the tensor pipe and HBM overlap
+      for (int i = threadIdx.x; i < nseg; i += kThreads) {
+        const int j = (i & 1) ? nseg - 1 - (i >> 1) : (i >> 1);
+        t_order[i] = static_cast<int>(keys[j] & 0xffffffffu);
+      }
+    } else {
+      for (int i = threadIdx.x; i < nseg; i += kThreads)
+        t_order[i] = static_cast<int>(keys[i] & 0xffffffffu);
+    }
   } else {
     for (int i = threadIdx.x; i < nseg; i += kThreads) t_order[i] = i;
   }

@@ -349,6 +349,72 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same quantisation with one 256-thread block per row and the row held in registers
+// (cols <= kFp8RowRegCols): one HBM read of the row instead of a read for the amax and a second
+// for the conversion, and 8 independent 16-byte loads per thread in flight.
+constexpr int kFp8RowVecPerThread = 8;
+constexpr int kFp8RowRegCols = 256 * kFp8RowVecPerThread * 8;  // 16384
+
+template <typename T16>
+__global__ void __launch_bounds__(256)
+    quantize_rows_fp8_reg_kernel(const T16* __restrict__ x, int cols, uint8_t* __restrict__ q,
+                                 float* __restrict__ scale) {
+  __shared__ float s_max[8];
+  const int r = blockIdx.x;
+  const int vec = cols / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * cols);
+  uint4 v[kFp8RowVecPerThread];
+#pragma unroll
+  for (int i = 0; i < kFp8RowVecPerThread; ++i) {
+    const int c = threadIdx.x + i * 256;
+    v[i] = c < vec ? xr[c] : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFp8RowVecPerThread; ++i) {
+    float f[8];
+    unpack8<T16>(v[i], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = amax;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < 8; ++w) amax = fmaxf(amax, s_max[w]);
+  const float s = amax > 0.f ? amax / 448.f : 1.f;
+  if (threadIdx.x == 0) scale[r] = s;
+  // x / s, correctly rounded, without a division per element (Markstein, IBM J. Res. Dev. 34(1),
+  // 1990): with y = RN(1/s) and q0 = RN(x y), the fma residual r = x - s q0 is exact and
+  // RN(q0 + r y) = RN(x / s) when no underflow occurs; |x / s| <= 448 here, and quotients small
+  // enough to underflow round to zero in e4m3 either way.
+  const float y = __frcp_rn(s);
+  uint2* qr = reinterpret_cast<uint2*>(q + static_cast<size_t>(r) * cols);
+#pragma unroll
+  for (int i = 0; i < kFp8RowVecPerThread; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c >= vec) break;
+    float f[8];
+    unpack8<T16>(v[i], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float q0 = f[e] * y;
+      f[e] = fmaf(fmaf(-s, q0, f[e]), y, q0);
+    }
+    uint32_t w[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+          make_float2(f[4 * h], f[4 * h + 1]), __NV_SATFINITE, __NV_E4M3);
+      const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+          make_float2(f[4 * h + 2], f[4 * h + 3]), __NV_SATFINITE, __NV_E4M3);
+      w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+    qr[c] = make_uint2(w[0], w[1]);
+  }
+}
+
 // ---------------------------------------------------------------- MX (block-scaled) quantisation
 // OCP MX e4m3 with UE8M0 scales, one per 32 consecutive elements of a row. For each group of 32:
 // amax = max |x|, E = floor(log2 amax), scale exponent X = E - 8, plus 1 when amax / 2^E > 1.75
@@ -360,6 +426,10 @@ __global__ void __launch_bounds__(256)
 // (0..3) sit at byte (r % 32) * 16 + (r / 32) * 4 + j. Bytes of padding rows are not written.
 constexpr int kMxMaxSegments = 1024;
 
+// One warp per row (grid-stride over rows). Lane l converts 8 consecutive elements per step, so a
+// 32-element group is four lanes and one warp step covers 256 elements with fully coalesced 16-B
+// loads and 8-B stores; the group amax is two shuffles. The row's segment, scale block and row in
+// block are found once per row.
 template <typename T16>
 __global__ void __launch_bounds__(256)
     quantize_mxfp8_kernel(const T16* __restrict__ x, const int64_t* __restrict__ counts, int nseg,
@@ -394,53 +464,61 @@ __global__ void __launch_bounds__(256)
     if (lane == 0) s_rowoff[nseg] = carry;
   }
   __syncthreads();
-  const int ng = k / 32, kg = k / 128;
+  const int lane = threadIdx.x & 31;
+  const int kg = k / 128;
   const int covered = s_rowoff[nseg];
-  const long long total = static_cast<long long>(rows) * ng;
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * 256) {
-    const int r = static_cast<int>(i / ng), j = static_cast<int>(i % ng);
-    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * k + j * 32);
-    float f[32];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      float g[8];
-      unpack8<T16>(src[u], g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[8 * u + e] = g[e];
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(f[e]));
-    const uint32_t bits = __float_as_uint(amax);
-    const int eb = static_cast<int>((bits >> 23) & 0xFFu);
-    int xe = eb == 0 ? -127 : eb - 127 - 8 + ((bits & 0x7FFFFFu) > 0x600000u ? 1 : 0);
-    xe = xe < -127 ? -127 : (xe > 127 ? 127 : xe);
-    const float inv = xe <= 126 ? __uint_as_float(static_cast<uint32_t>(127 - xe) << 23)
-                                : __uint_as_float(1u << 22);  // 2^-127
-    uint32_t w[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-          make_float2(f[4 * h] * inv, f[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
-      const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-          make_float2(f[4 * h + 2] * inv, f[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
-      w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(q + static_cast<size_t>(r) * k + j * 32);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    if (r < covered) {
+  const int nwarps = gridDim.x * 8;
+  for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    // scale-block coordinates of row r (rows past the counted ones get no scale bytes)
+    size_t sf_row = 0;
+    const bool has_sf = r < covered;
+    if (has_sf) {
       int lo = 0, hi = nseg - 1;  // the last segment starting at or before r is r's segment
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (s_rowoff[mid] <= r) lo = mid; else hi = mid - 1;
       }
       const int rl = r - s_rowoff[lo];
-      const int blk = s_blkoff[lo] + rl / 128;
       const int rr = rl & 127;
-      sf[(static_cast<size_t>(blk) * kg + j / 4) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (j & 3)] =
-          static_cast<uint8_t>(xe + 127);
+      sf_row = static_cast<size_t>(s_blkoff[lo] + rl / 128) * kg * 512 + (rr & 31) * 16 +
+               (rr >> 5) * 4;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * k);
+    uint2* dst = reinterpret_cast<uint2*>(q + static_cast<size_t>(r) * k);
+    const int vec = k / 8;
+    // every lane runs every step (the shuffles need the whole warp); vec is a multiple of 16, so
+    // a step's inactive lanes are whole groups
+#pragma unroll 2
+    for (int c0 = 0; c0 < vec; c0 += 32) {
+      const int c = c0 + lane;  // 8-element chunk; group j = c / 4
+      const bool active = c < vec;
+      float f[8];
+      unpack8<T16>(active ? src[c] : make_uint4(0, 0, 0, 0), f);
+      float amax = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      const uint32_t bits = __float_as_uint(amax);
+      const int eb = static_cast<int>((bits >> 23) & 0xFFu);
+      int xe = eb == 0 ? -127 : eb - 127 - 8 + ((bits & 0x7FFFFFu) > 0x600000u ? 1 : 0);
+      xe = xe < -127 ? -127 : (xe > 127 ? 127 : xe);
+      const float inv = xe <= 126 ? __uint_as_float(static_cast<uint32_t>(127 - xe) << 23)
+                                  : __uint_as_float(1u << 22);  // 2^-127
+      uint32_t w[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+            make_float2(f[4 * h] * inv, f[4 * h + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+            make_float2(f[4 * h + 2] * inv, f[4 * h + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+        w[h] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      if (!active) continue;
+      dst[c] = make_uint2(w[0], w[1]);
+      const int j = c >> 2;
+      if (has_sf && (c & 3) == 0)
+        sf[sf_row + static_cast<size_t>(j >> 2) * 512 + (j & 3)] = static_cast<uint8_t>(xe + 127);
     }
   }
 }
@@ -624,6 +702,18 @@ int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dty
   if (cols % 16 || !ggo::aligned16(x_dev) || !ggo::aligned16(q_dev)) return GGO_ERR_ALIGNMENT;
   if (rows > INT32_MAX || cols > INT32_MAX) return GGO_ERR_SHAPE;
   if (rows == 0) return GGO_OK;
+  if (cols <= ggo::kFp8RowRegCols) {  // the row fits in the block's registers
+    const int grid = static_cast<int>(rows);
+    if (dtype == GGO_DTYPE_BF16)
+      ggo::quantize_rows_fp8_reg_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x_dev), static_cast<int>(cols),
+          static_cast<uint8_t*>(q_dev), scale_dev);
+    else
+      ggo::quantize_rows_fp8_reg_kernel<__half><<<grid, 256, 0, stream>>>(
+          static_cast<const __half*>(x_dev), static_cast<int>(cols), static_cast<uint8_t*>(q_dev),
+          scale_dev);
+    return ggo::check_launch();
+  }
   const int grid = static_cast<int>((rows + 7) / 8);
   if (dtype == GGO_DTYPE_BF16)
     ggo::quantize_rows_fp8_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
@@ -647,8 +737,7 @@ int ggo_quantize_mxfp8(const void* x_dev, int dtype, const int64_t* counts_dev, 
   if (k % 128 || !ggo::aligned16(x_dev) || !ggo::aligned16(q_dev)) return GGO_ERR_ALIGNMENT;
   if (rows > INT32_MAX || k > INT32_MAX) return GGO_ERR_SHAPE;
   if (rows == 0) return GGO_OK;
-  const long long groups = rows * (k / 32);
-  const long long want = (groups + 255) / 256;
+  const long long want = (rows + 7) / 8;  // one warp per row, grid-stride beyond 4096 blocks
   const int grid = static_cast<int>(want < 4096 ? want : 4096);
   if (dtype == GGO_DTYPE_BF16)
     ggo::quantize_mxfp8_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(

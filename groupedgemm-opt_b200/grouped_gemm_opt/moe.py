@@ -402,7 +402,8 @@ def quantize_moe_weights(w_gate_up: torch.Tensor, w_down: torch.Tensor) -> MoEFP
 
 
 def fused_moe_fp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: MoEFP8Weights,
-                  top_k: int, sort_by_m: bool = True) -> torch.Tensor:
+                  top_k: int, sort_by_m: bool = True,
+                  timer: Optional[StageEvents] = None) -> torch.Tensor:
     """Single-GPU MoE layer with FP8 (e4m3) grouped GEMMs: route -> dispatch -> per-row
     quantisation of the gathered rows -> gate/up GEMM with a scaled SwiGLU epilogue (bf16 h) ->
     per-row quantisation of h -> down GEMM with a scaled epilogue -> combine. Routing, dispatch
@@ -410,14 +411,24 @@ def fused_moe_fp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: Mo
     from grouped_gemm_opt._native import _C
     E = router_logits.size(1)
     assert weights.w_gate_up_q.size(0) == E, "all experts must be local"
+    if timer is not None:
+        timer.start()
     ids, w, tpe, scratch = _C.moe_route(router_logits, top_k)
+    _mark(timer, "route")
     xs, _, slot_pos = _C.moe_permute(hidden.contiguous(), ids, scratch, E)
+    _mark(timer, "dispatch")
     xq, xsc = _C.quantize_fp8_rows(xs)
+    _mark(timer, "quantize_x")
     h = _C.grouped_gemm_swiglu_fp8(xq, xsc, weights.w_gate_up_q, weights.w_gate_up_scale, tpe, E,
                                    sort_by_m)
+    _mark(timer, "gate_up")
     hq, hsc = _C.quantize_fp8_rows(h)
+    _mark(timer, "quantize_h")
     y = _C.grouped_gemm_fp8(hq, hsc, weights.w_down_q, weights.w_down_scale, tpe, 4, sort_by_m)
-    return _C.moe_combine(y, w, slot_pos)
+    _mark(timer, "down")
+    out = _C.moe_combine(y, w, slot_pos)
+    _mark(timer, "combine")
+    return out
 
 
 @dataclass
@@ -440,19 +451,30 @@ def quantize_moe_weights_mxfp8(w_gate_up: torch.Tensor, w_down: torch.Tensor) ->
 
 
 def fused_moe_mxfp8(hidden: torch.Tensor, router_logits: torch.Tensor, weights: MoEMXFP8Weights,
-                    top_k: int, sort_by_m: bool = True) -> torch.Tensor:
+                    top_k: int, sort_by_m: bool = True,
+                    timer: Optional[StageEvents] = None) -> torch.Tensor:
     """Single-GPU MoE layer with MXFP8 grouped GEMMs: route -> dispatch -> MX quantisation of the
     gathered rows -> gate/up GEMM with the SwiGLU epilogue (bf16 h) -> MX quantisation of h ->
     down GEMM -> combine. Routing, dispatch and combine are the bf16 layer's."""
     from grouped_gemm_opt._native import _C
     E = router_logits.size(1)
     assert weights.w_gate_up_q.size(0) == E, "all experts must be local"
+    if timer is not None:
+        timer.start()
     ids, w, tpe, scratch = _C.moe_route(router_logits, top_k)
+    _mark(timer, "route")
     xs, _, slot_pos = _C.moe_permute(hidden.contiguous(), ids, scratch, E)
+    _mark(timer, "dispatch")
     xq, xsc = _C.quantize_mxfp8(xs, tpe)
+    _mark(timer, "quantize_x")
     h = _C.grouped_gemm_swiglu_mxfp8(xq, xsc, weights.w_gate_up_q, weights.w_gate_up_scale, tpe,
                                      E, weights.F, sort_by_m)
+    _mark(timer, "gate_up")
     hq, hsc = _C.quantize_mxfp8(h, tpe)
+    _mark(timer, "quantize_h")
     y = _C.grouped_gemm_mxfp8(hq, hsc, weights.w_down_q, weights.w_down_scale, tpe, E, sort_by_m)
-    return _C.moe_combine(y, w, slot_pos)
+    _mark(timer, "down")
+    out = _C.moe_combine(y, w, slot_pos)
+    _mark(timer, "combine")
+    return out
 

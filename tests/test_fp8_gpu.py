@@ -106,3 +106,16 @@ def test_fp8_cfg2_full_size_sampled():
         b = wq[e].float().cpu() * ws[e].cpu().unsqueeze(1)
         ref.append(b @ a)
     assert_parity(out[rows.to(DEV)], torch.stack(ref), "fp8 cfg2")
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 14336), (5, 16384), (3, 16400), (64, 1040), (9, 16)])
+def test_quantize_bit_exact_row_widths(rows, cols):
+    """Both quantiser forms: rows held in registers (cols <= 16384) and the two-pass one."""
+    from grouped_gemm_opt import quantize_fp8
+    g = torch.Generator().manual_seed(cols)
+    x = (torch.randn(rows, cols, generator=g) * torch.logspace(-2, 2, rows).unsqueeze(1)).to(
+        torch.bfloat16)
+    q, s = quantize_fp8(x.to(DEV))
+    rq, rs = _ref_quant(x)
+    assert torch.equal(s.cpu(), rs)
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))

@@ -144,3 +144,16 @@ def test_mxfp8_large_k_many_tiles():
     wd = _deq(wq, ws, [N] * len(counts), K).view(len(counts), N, K)
     assert_parity(out, oracle.sequential_gemm(xd, wd, tpe), "mxfp8 large")
 
+
+
+@pytest.mark.parametrize("counts,k", [([3, 0, 250], 384), ([130, 1], 14336), ([40], 128)])
+def test_quantize_mxfp8_bit_exact_widths(counts, k):
+    """Row widths whose last warp step is partial (K % 256 == 128) and the Mixtral F width."""
+    from grouped_gemm_opt import quantize_mxfp8
+    g = torch.Generator().manual_seed(k)
+    T = sum(counts)
+    x = (torch.randn(T, k, generator=g) * torch.logspace(-3, 3, T).unsqueeze(1)).to(torch.bfloat16)
+    q, sf = quantize_mxfp8(x.to(DEV), torch.tensor(counts).to(DEV))
+    rq, rsf = oracle.mx_quantize(x, counts)
+    assert torch.equal(q.cpu().view(torch.uint8), rq)
+    assert np.array_equal(sf.cpu().numpy(), rsf)
