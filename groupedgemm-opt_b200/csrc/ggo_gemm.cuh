@@ -436,6 +436,44 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
   constexpr int OUTW = epi_glu(EPI) ? BN / 2 : BN;
   const int lane = threadIdx.x & 31;
   const uint32_t st_row = smem_u32(stage) + lane * 128;
+  if (warp_tma && OUTW % 64 == 0) {
+    // TMA-store path, software-pipelined: box i+1 is read from TMEM (and converted) while the
+    // bulk store of box i still reads the staging buffer, so the two latencies overlap instead of
+    // adding up box after box.
+    uint32_t o[32];
+    load_out32<BN, EPI, BF16>(t_row, 0, *reinterpret_cast<uint32_t(*)[16]>(o), rs,
+                              cs_row ? cs_row + n0 : nullptr, n_out - n0, cs_up_off);
+    load_out32<BN, EPI, BF16>(t_row, 32, *reinterpret_cast<uint32_t(*)[16]>(o + 16), rs,
+                              cs_row ? cs_row + n0 + 32 : nullptr, n_out - (n0 + 32), cs_up_off);
+#pragma unroll 1
+    for (int c64 = 0; c64 < OUTW; c64 += 64) {
+      if (c64 > 0) {  // the previous box's store has read the staging buffer
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t chunk = static_cast<uint32_t>(q ^ (lane & 7));
+        st_shared_v4(st_row + chunk * 16, o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, stage, n0 + c64, x_row0);
+        bulk_commit();
+      }
+      const int nx = c64 + 64;
+      if (nx < OUTW) {
+        load_out32<BN, EPI, BF16>(t_row, nx, *reinterpret_cast<uint32_t(*)[16]>(o), rs,
+                                  cs_row ? cs_row + n0 + nx : nullptr, n_out - (n0 + nx),
+                                  cs_up_off);
+        load_out32<BN, EPI, BF16>(t_row, nx + 32, *reinterpret_cast<uint32_t(*)[16]>(o + 16), rs,
+                                  cs_row ? cs_row + n0 + nx + 32 : nullptr,
+                                  n_out - (n0 + nx + 32), cs_up_off);
+      }
+    }
+    return;
+  }
   const bool staged = warp_tma || row_copy;
 #pragma unroll 1
   for (int c64 = 0; c64 < OUTW; c64 += 64) {
