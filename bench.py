@@ -375,9 +375,13 @@ def mixtral_layer_leg(world, rank, local, steps, warmup):
                 "kernel": "grouped_gemm_pair_kernel SwiGLU (gate/up; + its short-tail pass), "
                           "device time per layer from CUDA events around the launch",
                 "algorithmic_flop_per_launch": [2.0 * r * 2 * F * H for r in rows],
-                "achieved_per_rank": ach,
-                "traffic": _traffic(f"moe_gate_up_ep{world}") or
-                (_traffic("moe_gate_up_ep1") if world == 1 else None)}
+                "achieved_per_rank": ach}
+    t1 = _traffic("moe_gate_up_ep1")
+    roofline["traffic"] = None if t1 is None else t1 / world
+    roofline["traffic_source"] = (
+        "ncu DRAM read+write of the gate/up launch at N=1 (profiles/traffic.txt)" if world == 1
+        else f"the N=1 capture / {world}: a rank's launch processes 1/N of the rows and holds "
+             "1/N of the experts (not captured at this N)")
     # the whole layer's roofline: FLOPs at the sustained peak vs bytes over NVLink
     t_flop = MIX_FLOP / world / (peak * 1e12) * 1e3
     nvl_bytes = 2.0 * tl * k * H * 2 * (world - 1) / world
