@@ -57,10 +57,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // MX: the scales of consecutive K steps rotate through 16-column TMEM slots (A: 4 columns, B:
   // 4 per atom) in the gaps beside the two accumulators (columns BN..255 and 256+BN..511), so
   // copying one step's scales never waits for the MMAs still reading the previous step's.
-  // Widths are multiples of 64, so B's scales start at an even column of the slot (0 or 2), the
-  // offsets the block-scaled MMA is used with here; a 224-wide variant (odd offsets, N = 224)
-  // stopped with a misaligned-address error and is not built.
-  static_assert(!MX || (FP8 && !BMN && BN <= 192 && BN % 64 == 0), "MX tile");
+  // The block-scaled pair MMA is used only with N in {64, 128, 192, 256} and with B's scales
+  // starting 0 or 2 TMEM words (0 or 64 weight rows) into a 128-row scale block: tiles start at
+  // multiples of their width inside an expert, so a width in {64, 128, 192} gives exactly those
+  // offsets (256 leaves no TMEM columns for the scale slots). A 224-wide variant (N = 224, offsets
+  // 1 and 3) stopped with a misaligned-address error and is not built.
+  static_assert(!MX || (FP8 && !BMN && (BN == 64 || BN == 128 || BN == 192)), "MX tile width");
   static_assert(!MX || 4 + 4 * L::kSfbAtoms <= 16, "scale slot width");
   constexpr uint32_t kSfSlotsPerGap = (256 - BN) / 16;
   constexpr uint32_t kSfSlots = 2 * kSfSlotsPerGap;
