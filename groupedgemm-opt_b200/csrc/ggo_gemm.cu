@@ -15,6 +15,7 @@
 #include "ggo_gemm.cuh"
 #include "ggo_gemm_pair.cuh"
 #include "ggo_gemm_wgrad.cuh"
+#include "ggo_gemm_wgrad_pair.cuh"
 #include "ggo_internal.h"
 
 namespace ggo {
@@ -500,6 +501,25 @@ int launch_wgrad(const void* x, const void* dy, void* dw, const WgradParams& p, 
   return check_launch();
 }
 
+template <bool BF16>
+int launch_wgrad_pair(const void* x, const void* dy, void* dw, const WgradParams& p, int dev,
+                      cudaStream_t stream) {
+  CUtensorMap mdy, mx, mw;
+  if (int st = make_map(&mdy, dy, p.rows, p.n, BF16, 64, 64)) return st;
+  if (int st = make_map(&mx, x, p.rows, p.k, BF16, 64, 64)) return st;
+  if (int st = make_map(&mw, dw, static_cast<int64_t>(p.num_experts) * p.n, p.k, BF16, 32, 64))
+    return st;
+  auto kern = grouped_gemm_wgrad_pair_kernel<BF16>;
+  constexpr int smem = WgradPairLayout::kTotal;
+  int clusters = 0;
+  if (int st = kernel_setup(kern, smem, dev, true, &clusters)) return st;
+  const int64_t tiles = static_cast<int64_t>(p.num_experts) * ((p.n + 255) / 256) *
+                        ((p.k + 255) / 256);
+  const int64_t pairs = tiles < clusters ? tiles : clusters;
+  kern<<<static_cast<int>(2 * pairs), kThreads, smem, stream>>>(mdy, mx, mw, p);
+  return check_launch();
+}
+
 int wgrad_common(const void* x, const void* dy, void* dw, const int64_t* counts, int num_experts,
                  int64_t rows, int64_t n, int64_t k, int dtype, int sort_by_m, void* workspace,
                  cudaStream_t stream) {
@@ -524,9 +544,17 @@ int wgrad_common(const void* x, const void* dy, void* dw, const int64_t* counts,
   p.out = dw;
   p.ws = static_cast<GgoWorkspace*>(workspace);
   p.wait_limit = GGO_WAIT_LIMIT_CYCLES;
-  // 128x256 tiles unless they leave SMs idle
+  // 256x256 CTA-pair tiles when they fill every SM pair, else single-CTA 128x256 tiles unless
+  // those leave SMs idle. GGO_WGRAD_PAIR: 0 never pairs, 2 always pairs (tests).
   const int64_t wide = static_cast<int64_t>(num_experts) * ((n + 127) / 128) * ((k + 255) / 256);
   const bool bf16 = dtype == GGO_DTYPE_BF16;
+  const int64_t pair_tiles =
+      static_cast<int64_t>(num_experts) * ((n + 255) / 256) * ((k + 255) / 256);
+  const char* pair_env = getenv("GGO_WGRAD_PAIR");
+  const int pair_mode = pair_env ? atoi(pair_env) : 1;
+  if (pair_mode == 2 || (pair_mode == 1 && pair_tiles >= g_sm_count[dev] / 2))
+    return bf16 ? launch_wgrad_pair<true>(x, dy, dw, p, dev, stream)
+                : launch_wgrad_pair<false>(x, dy, dw, p, dev, stream);
   if (wide >= g_sm_count[dev])
     return bf16 ? launch_wgrad<256, true>(x, dy, dw, p, dev, stream)
                 : launch_wgrad<256, false>(x, dy, dw, p, dev, stream);

@@ -269,9 +269,12 @@ def _wgrad_ref(x, dy, tpe):
                                         ([1, 7, 63, 64, 65, 130, 0], 200, 1000),
                                         ([4000, 3000], 512, 2048),
                                         ([0, 0, 5], 64, 64)])
-def test_wgrad(sort, counts, n, k):
-    """dw[e] = dy_e^T @ x_e over each expert's own tokens (zero for experts without tokens)."""
+@pytest.mark.parametrize("pair", ["0", "2"])
+def test_wgrad(sort, counts, n, k, pair, monkeypatch):
+    """dw[e] = dy_e^T @ x_e over each expert's own tokens (zero for experts without tokens), on
+    the single-CTA kernel and on the CTA-pair kernel (forced; AUTO pairs only large problems)."""
     from grouped_gemm_opt import _C
+    monkeypatch.setenv("GGO_WGRAD_PAIR", pair)
     g = torch.Generator().manual_seed(len(counts) * 7 + k)
     tpe = torch.tensor(counts)
     T = int(tpe.sum())
@@ -321,8 +324,9 @@ def test_split_tail_launch(ggo, split, monkeypatch):
 
 
 @pytest.mark.parametrize("tc", [1, 3])
-def test_dgrad_wgrad_fp16(tc):
+def test_dgrad_wgrad_fp16(tc, monkeypatch):
     from grouped_gemm_opt import _C
+    monkeypatch.setenv("GGO_WGRAD_PAIR", "2" if tc == 3 else "0")
     g = torch.Generator().manual_seed(tc)
     counts = [700, 0, 300, 1100, 20]
     tpe = torch.tensor(counts)
