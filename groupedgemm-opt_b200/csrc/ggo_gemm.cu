@@ -311,11 +311,11 @@ struct GemmExtras {
   const void* b_sf = nullptr;
 };
 
-// MX tiles: CTA pairs of 256 x 192 (the rest of each accumulator's 256 TMEM columns holds the
-// scales). SwiGLU weights for the MX path are blocked by kMxGluBlock output columns:
-// [E, 2 * F_pad, K], F_pad = F rounded up to kMxGluBlock, block j = gate rows j*96.. then the
-// matching up rows.
-constexpr int kMxPairBN = 192;
+// MX tiles: CTA pairs of 256 x 256 with overlapping accumulators (TMEM columns 0-255 and
+// 192-447; the scales in 448-511). SwiGLU weights for the MX path are blocked by kMxGluBlock
+// output columns: [E, 2 * F_pad, K], F_pad = F rounded up to kMxGluBlock, block j = gate rows
+// j*128.. then the matching up rows.
+constexpr int kMxPairBN = 256;
 constexpr int kMxGluBlock = kMxPairBN / 2;
 int64_t mx_glu_rows(int64_t f) { return 2 * ((f + kMxGluBlock - 1) / kMxGluBlock) * kMxGluBlock; }
 // 512-B scale atoms of `rows` rows in `segments` segments (each padded to 128 rows), K columns

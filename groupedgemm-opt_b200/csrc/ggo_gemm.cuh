@@ -79,7 +79,7 @@ struct GemmParams {
   int n_out;              // columns of `out` (N, or F for SwiGLU)
   int n_b;                // rows of one expert's W (N, or 2F for SwiGLU)
   int k;                  // K
-  int sort_by_m;          // 0 segment order; 1 heaviest first; 2 heaviest/lightest interleaved
+  int sort_by_m;          // 0 segment order; 1 heaviest first; 2 heavy and light tiles interleaved
   int group_m;            // m-tiles per raster group (>= 1)
   void* out;              // [rows, n_out], bf16 or fp16
   int rows_is_bound;      // 1: `rows` is a capacity; counts may sum to less (no mismatch error)
@@ -243,17 +243,8 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
         __syncthreads();
       }
     }
-    if (p.sort_by_m == 2) {
-      // interleave heaviest and lightest: compute-bound blocks of long segments run beside the
-      // weight-streaming blocks of short ones, so the tensor pipe and HBM overlap
-      for (int i = threadIdx.x; i < nseg; i += kThreads) {
-        const int j = (i & 1) ? nseg - 1 - (i >> 1) : (i >> 1);
-        t_order[i] = static_cast<int>(keys[j] & 0xffffffffu);
-      }
-    } else {
-      for (int i = threadIdx.x; i < nseg; i += kThreads)
-        t_order[i] = static_cast<int>(keys[i] & 0xffffffffu);
-    }
+    for (int i = threadIdx.x; i < nseg; i += kThreads)
+      t_order[i] = static_cast<int>(keys[i] & 0xffffffffu);
   } else {
     for (int i = threadIdx.x; i < nseg; i += kThreads) t_order[i] = i;
   }
@@ -277,7 +268,33 @@ __device__ __forceinline__ void build_segment_table(const GemmParams& p, uint8_t
       t_tileoff[nseg] = carry;
       *total_tiles_s = carry;
     }
+    // Tile-level interleave (sort_by_m == 2): the tiles of segments with at least one full row
+    // block ("heavy", compute-bound) alternate with those of shorter segments ("light",
+    // weight-streaming), so the tensor pipe and HBM work at the same time. total_tiles_s[1]
+    // receives the heavy tile count (the processing order is heaviest first), -1 for no interleave.
+    __syncwarp();
+    int h = 0;
+    if (p.sort_by_m == 2) {
+      for (int base = 0; base < nseg; base += 32) {
+        const int i = base + lane;
+        const unsigned heavy = __ballot_sync(0xffffffffu, i < nseg && t_cnt[t_order[i]] >= TILE_M);
+        h += __popc(heavy);
+        if (heavy != 0xffffffffu) break;
+      }
+    }
+    if (lane == 0) total_tiles_s[1] = (p.sort_by_m == 2 && h > 0 && h < nseg) ? t_tileoff[h] : -1;
   }
+}
+
+// Position in the heaviest-first tile order of the t-th claimed tile when heavy and light tiles
+// alternate (`heavy` = heavy tile count, -1: no interleave): heavy tiles are [0, heavy), light
+// ones [heavy, total); pairs (heavy i, light i) come first, then the longer list's remainder.
+__device__ __forceinline__ int interleave_tile(int t, int heavy, int total) {
+  if (heavy < 0) return t;
+  const int light = total - heavy;
+  const int m = heavy < light ? heavy : light;
+  if (t < 2 * m) return (t & 1) ? heavy + (t >> 1) : (t >> 1);
+  return heavy > light ? t - light : t;
 }
 
 // Maps flat tile index t (< total tiles) to its rows, output columns and weight rows.
@@ -432,22 +449,37 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
                                                 const CUtensorMap* tmC, uint8_t* stage,
                                                 int x_row0, float rs = 1.f,
                                                 const float* cs_row = nullptr,
-                                                int cs_up_off = 0, bool row_copy = false) {
+                                                int cs_up_off = 0, bool row_copy = false,
+                                                int first_box = 0, uint32_t release_bar = 0) {
   constexpr int OUTW = epi_glu(EPI) ? BN / 2 : BN;
+  constexpr int kBoxes = (OUTW + 63) / 64;
   const int lane = threadIdx.x & 31;
   const uint32_t st_row = smem_u32(stage) + lane * 128;
+  // Output boxes run from `first_box` round to first_box - 1. With `release_bar` (a cluster
+  // address) the warp arrives on it once the first box's TMEM columns are read.
+  auto release = [&]() {
+    if (release_bar != 0u) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(release_bar);
+    }
+  };
   if (warp_tma && OUTW % 64 == 0) {
     // TMA-store path, software-pipelined: box i+1 is read from TMEM (and converted) while the
     // bulk store of box i still reads the staging buffer, so the two latencies overlap instead of
     // adding up box after box.
     uint32_t o[32];
-    load_out32<BN, EPI, BF16>(t_row, 0, *reinterpret_cast<uint32_t(*)[16]>(o), rs,
-                              cs_row ? cs_row + n0 : nullptr, n_out - n0, cs_up_off);
-    load_out32<BN, EPI, BF16>(t_row, 32, *reinterpret_cast<uint32_t(*)[16]>(o + 16), rs,
-                              cs_row ? cs_row + n0 + 32 : nullptr, n_out - (n0 + 32), cs_up_off);
+    const int f64 = 64 * first_box;
+    load_out32<BN, EPI, BF16>(t_row, f64, *reinterpret_cast<uint32_t(*)[16]>(o), rs,
+                              cs_row ? cs_row + n0 + f64 : nullptr, n_out - (n0 + f64), cs_up_off);
+    load_out32<BN, EPI, BF16>(t_row, f64 + 32, *reinterpret_cast<uint32_t(*)[16]>(o + 16), rs,
+                              cs_row ? cs_row + n0 + f64 + 32 : nullptr, n_out - (n0 + f64 + 32),
+                              cs_up_off);
+    release();
 #pragma unroll 1
-    for (int c64 = 0; c64 < OUTW; c64 += 64) {
-      if (c64 > 0) {  // the previous box's store has read the staging buffer
+    for (int b = 0; b < kBoxes; ++b) {
+      const int c64 = 64 * ((first_box + b) % kBoxes);
+      if (b > 0) {  // the previous box's store has read the staging buffer
         if (lane == 0) bulk_wait_read_all();
         __syncwarp();
       }
@@ -462,8 +494,8 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
         tma_store_2d(tmC, stage, n0 + c64, x_row0);
         bulk_commit();
       }
-      const int nx = c64 + 64;
-      if (nx < OUTW) {
+      const int nx = 64 * ((first_box + b + 1) % kBoxes);
+      if (b + 1 < kBoxes) {
         load_out32<BN, EPI, BF16>(t_row, nx, *reinterpret_cast<uint32_t(*)[16]>(o), rs,
                                   cs_row ? cs_row + n0 + nx : nullptr, n_out - (n0 + nx),
                                   cs_up_off);
@@ -476,8 +508,9 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
   }
   const bool staged = warp_tma || row_copy;
 #pragma unroll 1
-  for (int c64 = 0; c64 < OUTW; c64 += 64) {
-    if (warp_tma && c64 > 0) {  // the previous box's store has read the staging buffer
+  for (int b = 0; b < kBoxes; ++b) {
+    const int c64 = 64 * ((first_box + b) % kBoxes);
+    if (warp_tma && b > 0) {  // the previous box's store has read the staging buffer
       if (lane == 0) bulk_wait_read_all();
       __syncwarp();
     }
@@ -504,6 +537,7 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
         }
       }
     }
+    if (b == 0) release();
     if (warp_tma) {
       fence_proxy_async_smem();
       __syncwarp();
@@ -652,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
+  const int heavy_tiles = total_tiles_s[1];
   // K elements per pipeline stage: one 128-B swizzle row (64 bf16/fp16 or 128 e4m3)
   constexpr int kStageK = FP8 ? 128 : kBK;
   const int num_kb = (p.k + kStageK - 1) / kStageK;
@@ -667,7 +702,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         TileInfo info;
         info.rows = 0;
         if (t < total_tiles)
-          info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(t, p, t_cnt, t_rowoff, t_order, t_tileoff);
+          info = decode_tile<kBM, kOutBN, EPI, 128, BMN>(interleave_tile(t, heavy_tiles, total_tiles),
+                                                        p, t_cnt, t_rowoff, t_order, t_tileoff);
         info.skinny = (kSkinnyOk && info.rows > 0 && info.rows <= p.skinny_max) ? 1 : 0;
         if (!mbar_wait(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer)) break;
         ring[q] = info;

@@ -25,9 +25,10 @@ struct PairLayout {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 A rows
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's half of the BN-row B tile
   // MX: this CTA's A scales (one 512-B atom: 128 rows x 4 K groups of 32) and the scales of the
-  // weight rows from the 128-row block where the tile's B rows start (kSfbAtoms atoms: a tile
-  // width that is a multiple of 64 starts 0 or 64 rows into a block), behind the B half
-  static constexpr int kSfbAtoms = (64 + BN + 127) / 128;
+  // weight rows from the 128-row block where the tile's B rows start (kSfbAtoms atoms: a width
+  // that is a multiple of 128 starts on a block, a multiple of 64 0 or 64 rows into one), behind
+  // the B half
+  static constexpr int kSfbAtoms = BN % 128 == 0 ? BN / 128 : (64 + BN + 127) / 128;
   static constexpr int kSfBytes = MX ? (1 + kSfbAtoms) * 512 : 0;
   static constexpr int kTxBytes = kABytes + kBBytes + kSfBytes;  // one CTA's loads per stage
   static constexpr int kStageBytes = (kTxBytes + 1023) / 1024 * 1024;  // 1024-B aligned stages
@@ -62,16 +63,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // multiples of their width inside an expert, so a width in {64, 128, 192} gives exactly those
   // offsets (256 leaves no TMEM columns for the scale slots). A 224-wide variant (N = 224, offsets
   // 1 and 3) stopped with a misaligned-address error and is not built.
-  static_assert(!MX || (FP8 && !BMN && (BN == 64 || BN == 128 || BN == 192)), "MX tile width");
+  static_assert(!MX || (FP8 && !BMN && (BN == 64 || BN == 128 || BN == 192 || BN == 256)),
+                "MX tile width");
   static_assert(!MX || 4 + 4 * L::kSfbAtoms <= 16, "scale slot width");
-  constexpr uint32_t kSfSlotsPerGap = (256 - BN) / 16;
-  constexpr uint32_t kSfSlots = 2 * kSfSlotsPerGap;
+  // MX with 256-wide tiles: the two accumulators overlap by 64 TMEM columns (columns 0-255 and
+  // 192-447), which leaves columns 448-511 for four scale slots. The epilogue reads the overlapped
+  // 64 columns of a tile first and then releases the next tile's MMAs (which overwrite them), and
+  // drains the other 192 columns while those MMAs run.
+  constexpr bool kOverlap = MX && BN == 256;
+  constexpr uint32_t kSfSlotsPerGap = kOverlap ? 4 : (256 - BN) / 16;
+  constexpr uint32_t kSfSlots = kOverlap ? 4 : 2 * kSfSlotsPerGap;
   static_assert(!MX || kSfSlots >= 2, "scale slots");
   constexpr int S = L::kStages;
   // BN = N of the pair tile = columns of each CTA's accumulator (multiple of 32, <= 256)
   static_assert(BN % 32 == 0 && BN <= 256 && (EPI == kEpiStore || BN % 64 == 0), "tile width");
   constexpr int kTileM = 256;
-  constexpr int kAccStride = 256;        // TMEM columns between the two accumulators
+  constexpr int kAccStride = kOverlap ? 192 : 256;  // TMEM columns between the accumulators
   constexpr int kTmemCols = 512;
   constexpr int kOutBN = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
   constexpr bool kTmaStoreOk = kOutBN % 64 == 0;  // output boxes are 64 columns wide
@@ -151,6 +158,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = *total_tiles_s;
+  const int heavy_tiles = total_tiles_s[1];
   constexpr int kStageK = FP8 ? 128 : kBK;  // K elements per stage (one 128-B swizzle row)
   const int num_kb = (p.k + kStageK - 1) / kStageK;
 
@@ -166,7 +174,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int t = atomicAdd(&p.ws->tile_counter, 1);
           info.rows = 0;
           if (t < total_tiles)
-            info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(t, p, t_cnt, t_rowoff, t_order,
+            info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(
+                interleave_tile(t, heavy_tiles, total_tiles), p, t_cnt, t_rowoff, t_order,
                                                                t_tileoff);
           if (!mbar_wait_cluster(&sche_bar[q], qphase ^ 1, guard, err, kDevTimeoutProducer))
             break;
@@ -247,6 +256,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       static_assert(!BMN || (BN / 2) % 64 == 0, "MN-major B halves are whole 64-column boxes");
       int stage = 0, phase = 0, q = 0, qphase = 0, acc = 0, aphase = 0;
       uint32_t sf_slot = 0;  // MX: scale slot of the next K step
+      int tiles_done = 0;    // overlapped accumulators: tiles issued so far
       const uint32_t tiles_addr = smem_u32(tiles);
       while (true) {
         if (!mbar_wait_cluster(&schf_bar[q], qphase, guard, err, kDevTimeoutMma)) break;
@@ -255,7 +265,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_arrive(&sche_bar[q]);
         if (++q == kSchedDepth) { q = 0; qphase ^= 1; }
         if (!valid) break;
-        if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, guard, err, kDevTimeoutMma)) break;
+        if (kOverlap) {
+          // the previous tile's overlapped columns are read (and, the epilogue being in tile
+          // order, every column of the tile before it); acce_bar[0] completes once per tile
+          if (tiles_done > 0 && !mbar_wait_cluster(&acce_bar[0], (tiles_done - 1) & 1, guard, err,
+                                                   kDevTimeoutMma))
+            break;
+          ++tiles_done;
+        } else if (!mbar_wait_cluster(&acce_bar[acc], aphase ^ 1, guard, err, kDevTimeoutMma)) {
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccStride;
         bool ok = true;
@@ -274,7 +293,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // scales of this stage into TMEM (in order with the MMAs below and the previous
             // stage's): A's 128 rows, then B's rows as kSfbAtoms 4-column atoms
             const uint32_t sf_addr = a_addr + L::kABytes + L::kBBytes;
-            const uint32_t kSfaCol = sf_slot < kSfSlotsPerGap
+            const uint32_t kSfaCol = kOverlap ? 448u + 16u * sf_slot
+                                     : sf_slot < kSfSlotsPerGap
                                          ? BN + 16u * sf_slot
                                          : 256u + BN + 16u * (sf_slot - kSfSlotsPerGap);
             const uint32_t kSfbCol = kSfaCol + 4;
@@ -337,12 +357,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // column scales: one per weight row, [E, n_b] (gate rows then up rows for SwiGLU)
       const float* cs_row =
           kScaled ? p.col_scale + static_cast<size_t>(info.seg % p.num_experts) * p.n_b : nullptr;
+      // overlapped accumulators: the columns shared with the other accumulator first (the last
+      // 64 of accumulator 0, the first 64 of accumulator 1), then release the next tile's MMAs
+      constexpr int kBoxes = (EPI == kEpiSwiGLU ? BN / 2 : BN) / 64;
       store_tile_rows<BN, EPI, BF16>(t_row, info.n0, p.n_out, row_ok, out_row, warp_tma, &tmC,
                                      staging + ew * 4096, info.row0 + wrow0, rs, cs_row,
-                                     p.n_b / 2, p.origin != nullptr);
+                                     p.n_b / 2, p.origin != nullptr,
+                                     kOverlap ? (acc == 0 ? kBoxes - 1 : 0) : 0,
+                                     kOverlap ? mapa_shared(&acce_bar[0], 0) : 0u);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));
+      if (!kOverlap && lane == 0) mbar_arrive_cluster(mapa_shared(&acce_bar[acc], 0));
       if (++acc == 2) { acc = 0; aphase ^= 1; }
     }
   }

@@ -198,7 +198,7 @@ def grouped_gemm_opt_mxfp8(
     """MXFP8 grouped GEMM: ``out[i] = sum_k (q_in[i,k] 2^s_in[i,k//32]) (q_w[e,n,k] 2^s_w[e,n,k//32])``
     in bf16, the block scales applied by the tensor cores (tcgen05 kind::mxf8f6f4.block_scale,
     fp32 accumulation). Operands and scales come from :func:`quantize_mxfp8` (the input quantised
-    with the same ``tokens_per_expert``). Always runs 256 x 192 CTA-pair tiles: there is no tile
+    with the same ``tokens_per_expert``). Always runs 256 x 256 CTA-pair tiles: there is no tile
     configuration for the MX path."""
     assert input_q.is_cuda and weights_q.is_cuda
     tokens_per_expert = tokens_per_expert.to(torch.int64).contiguous()
@@ -213,18 +213,19 @@ def grouped_gemm_opt_mxfp8(
 
 def mxfp8_block_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
     """Reorders a gate/up weight [E, 2F, K] (gate rows then up rows) into the blocked layout the
-    MXFP8 SwiGLU GEMM reads: [E, 2 * F_pad, K], F_pad = F rounded up to 96, block j = gate rows
-    96j..96j+95 then the matching up rows, zero rows past F. A one-time weight preparation."""
+    MXFP8 SwiGLU GEMM reads: [E, 2 * F_pad, K], F_pad = F rounded up to 128, block j = gate rows
+    128j..128j+127 then the matching up rows, zero rows past F. A one-time weight preparation."""
     E, two_f, K = w_gate_up.shape
     F = two_f // 2
     rows = _C.mxfp8_glu_rows(F)
     fp = rows // 2
-    out = w_gate_up.new_zeros(E, fp // 96, 2, 96, K)
+    blk = 128
+    out = w_gate_up.new_zeros(E, fp // blk, 2, blk, K)
     g = w_gate_up.new_zeros(E, fp, K)
     g[:, :F] = w_gate_up[:, :F]
-    out[:, :, 0] = g.view(E, fp // 96, 96, K)
+    out[:, :, 0] = g.view(E, fp // blk, blk, K)
     g.zero_()
     g[:, :F] = w_gate_up[:, F:]
-    out[:, :, 1] = g.view(E, fp // 96, 96, K)
+    out[:, :, 1] = g.view(E, fp // blk, blk, K)
     return out.view(E, rows, K)
 

@@ -162,7 +162,7 @@ int ggo_quantize_fp8_rows(const void* x_dev, int64_t rows, int64_t cols, int dty
  * scales (tcgen05 kind::mxf8f6f4.block_scale) and accumulate in fp32. The GEMMs accept any UE8M0
  * scales; ggo_quantize_mxfp8 picks them with a non-saturating rule (below) that differs from the
  * OCP MX v1.0 reference rule (floor(log2 amax) - emax, then clamping), so its scale bytes can
- * differ from other MX producers' by one. The MXFP8 GEMMs always run 256 x 192 CTA-pair tiles:
+ * differ from other MX producers' by one. The MXFP8 GEMMs always run 256 x 256 CTA-pair tiles:
  * they take no tile configuration.
  * Scale layout ("128x4 blocked"): the rows of each segment start a fresh 128-row block after the
  * blocks of the previous segments; block b and K group g (128 elements, 4 scales) form the 512-B
@@ -186,7 +186,7 @@ int ggo_quantize_mxfp8(const void* x_dev, int dtype, const int64_t* counts_dev, 
 /* MXFP8 grouped GEMM: out[r, n] = sum_k (a[r,k] 2^sa[r,k/32]) (b[e,n,k] 2^sb[e,n,k/32]) in bf16.
  * input_dev [T, K] and weights_dev [E, N, K] e4m3 with their scales from ggo_quantize_mxfp8
  * (the input quantised with these same segment counts). Segment s multiplies expert
- * s % num_experts. K a multiple of 128, N of 8. Runs 256 x 192 CTA-pair tiles. */
+ * s % num_experts. K a multiple of 128, N of 8. Runs 256 x 256 CTA-pair tiles. */
 int ggo_grouped_gemm_mxfp8(const void* input_dev, const void* input_scale_dev,
                            const void* weights_dev, const void* weight_scale_dev, void* output_dev,
                            const int64_t* tokens_per_segment_dev, int num_segments,
@@ -194,8 +194,8 @@ int ggo_grouped_gemm_mxfp8(const void* input_dev, const void* input_scale_dev,
                            int sort_by_m, void* workspace_dev, cudaStream_t stream);
 
 /* Rows per expert of the blocked gate/up weight the MXFP8 SwiGLU GEMM reads: 2 * F_pad with
- * F_pad = F rounded up to 96. Block j (rows 192j .. 192j+191) holds gate rows 96j .. 96j+95 then
- * the matching up rows; rows past F are zero. */
+ * F_pad = F rounded up to 128. Block j (rows 256j .. 256j+255) holds gate rows 128j .. 128j+127
+ * then the matching up rows; rows past F are zero. */
 int64_t ggo_mxfp8_glu_rows(int64_t F);
 
 /* MXFP8 gate/up GEMM with the SwiGLU epilogue: h[r, f] = silu(g) * u, g / u the block-scaled

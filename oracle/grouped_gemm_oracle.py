@@ -274,7 +274,7 @@ def mx_dequantize(q: torch.Tensor, sf: np.ndarray, counts, k: int) -> torch.Tens
     return (qf.view(rows, k // 32, 32) * torch.from_numpy(scale).unsqueeze(-1)).view(rows, k)
 
 
-def mx_block_gate_up(w_gate_up: torch.Tensor, block: int = 96) -> torch.Tensor:
+def mx_block_gate_up(w_gate_up: torch.Tensor, block: int = 128) -> torch.Tensor:
     """[E, 2F, K] gate-then-up rows -> [E, 2 F_pad, K] blocked: block j = gate rows
     block*j.. then the matching up rows, zero rows past F (F_pad = F rounded up to `block`)."""
     E, two_f, K = w_gate_up.shape
@@ -288,7 +288,7 @@ def mx_block_gate_up(w_gate_up: torch.Tensor, block: int = 96) -> torch.Tensor:
     return out.reshape(E, 2 * fp, K)
 
 
-def mx_unblock_gate_up(w_blocked: torch.Tensor, f: int, block: int = 96) -> torch.Tensor:
+def mx_unblock_gate_up(w_blocked: torch.Tensor, f: int, block: int = 128) -> torch.Tensor:
     """Inverse of mx_block_gate_up: [E, 2 F_pad, K] blocked -> [E, 2F, K] gate-then-up."""
     E, rows, K = w_blocked.shape
     v = w_blocked.reshape(E, rows // (2 * block), 2, block, K)

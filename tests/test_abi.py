@@ -84,7 +84,7 @@ def test_mxfp8_metadata_and_validation(lib):
     assert lib.ggo_mxfp8_scale_bytes(256, 2, 100) == 0   # K must be a multiple of 128
     lib.ggo_mxfp8_glu_rows.restype = ctypes.c_int64
     lib.ggo_mxfp8_glu_rows.argtypes = [ctypes.c_int64]
-    assert lib.ggo_mxfp8_glu_rows(200) == 576 and lib.ggo_mxfp8_glu_rows(192) == 384
+    assert lib.ggo_mxfp8_glu_rows(200) == 512 and lib.ggo_mxfp8_glu_rows(256) == 512
     q = lib.ggo_quantize_mxfp8
     q.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
                   ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]

@@ -89,7 +89,7 @@ def test_mxfp8_segments_rank_major():
 
 def test_swiglu_mxfp8():
     from grouped_gemm_opt import _C, mxfp8_block_gate_up, quantize_mxfp8
-    counts, K, F = [2000, 0, 3000, 77], 256, 200   # F not a multiple of the 96-row block
+    counts, K, F = [2000, 0, 3000, 77], 256, 200   # F not a multiple of the 128-row block
     E = len(counts)
     x, w, tpe = gemm_inputs(counts, K, 2 * F, seed=2)
     wb = mxfp8_block_gate_up(w.to(DEV))

@@ -175,8 +175,9 @@ def test_mx_round_trip_error_bound():
 def test_mx_gate_up_blocking_round_trip():
     w = torch.randn(3, 2 * 200, 128)
     b = oracle.mx_block_gate_up(w)
-    assert b.shape == (3, 2 * 288, 128)
-    assert torch.equal(b[:, 96:192], w[:, 200:296])  # block 0: gate rows 0..95 then up rows 0..95
+    assert b.shape == (3, 2 * 256, 128)
+    # block 0: gate rows 0..127 then up rows 0..127
+    assert torch.equal(b[:, :128], w[:, :128]) and torch.equal(b[:, 128:256], w[:, 200:328])
     assert torch.equal(oracle.mx_unblock_gate_up(b, 200), w)
 
 
