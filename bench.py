@@ -430,7 +430,7 @@ def dsv3_leg(world, rank, local, steps, warmup):
     and the decode-like T=256 (tokens in total). N>1: fused expert-parallel path."""
     import torch
     import torch.distributed as dist
-    from grouped_gemm_opt import EPBuffers, fused_moe
+    from grouped_gemm_opt import EPBuffers, StageEvents, fused_moe
     H, F, Ex, k = 7168, 2048, 256, 8
     el = Ex // world
     wgu, wd = _local_weights(H, F, Ex, DSV3_SEED_EXPERTS, rank, world)
@@ -444,13 +444,25 @@ def dsv3_leg(world, rank, local, steps, warmup):
         x_g, l_g, x, logits = _tokens(T, H, Ex, DSV3_SEED_TOKENS + T, rank, world)
         bufs = EPBuffers(grp, tl, H, k, Ex, torch.bfloat16) if world > 1 else None
         holder = {}
+        timer = {"t": None}
 
         def fn():
-            holder["y"] = fused_moe(x, logits, wgu, wd, k, ep_group=grp, ep_buffers=bufs)
+            holder["y"] = fused_moe(x, logits, wgu, wd, k, ep_group=grp, ep_buffers=bufs,
+                                    timer=timer["t"])
 
         for _ in range(warmup):
             fn()
-        ms, _, clk = measure(fn, steps, world, local)
+        with ClockSampler(local) as clk_s:
+            _warm(fn, world, 1.0)
+            timer["t"] = StageEvents()
+            total_ms, _ = _timed(fn, steps, world)
+        clk = clk_s.summary()
+        ms = total_ms / steps
+        st = timer["t"].ms()
+        names = sorted(st)
+        per_rank = _gather_floats([st[n] / steps for n in names], world)
+        stages = {n: {"max_ms": max(pr[i] for pr in per_rank),
+                      "min_ms": min(pr[i] for pr in per_rank)} for i, n in enumerate(names)}
         if bufs is not None:
             bufs.check()
         wbytes = 3.0 * el * F * H * 2
@@ -462,7 +474,7 @@ def dsv3_leg(world, rank, local, steps, warmup):
                         "tflops": 6.0 * T * k * H * F / (ms / 1e3) / 1e12,
                         "weight_gbs_per_gpu": wbytes / (ms / 1e3) / 1e9,
                         "weight_hbm_frac": wbytes / (ms / 1e3) / 1e9 / hbm,
-                        "clocks": clk, "ep_parity": par}
+                        "stages_ms_per_layer": stages, "clocks": clk, "ep_parity": par}
         del x_g, l_g, x, logits, holder
         torch.cuda.empty_cache()
     return out

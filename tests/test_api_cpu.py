@@ -41,3 +41,28 @@ def test_fused_moe_shape_checks():
         fused_moe(x, torch.randn(4, 8), torch.randn(8, 32, 16), torch.randn(8, 16, 8), 9)
     with pytest.raises(AssertionError):  # wrong local expert count
         fused_moe(x, torch.randn(4, 8), torch.randn(4, 32, 16), torch.randn(4, 16, 8), 2)
+
+
+def test_bench_reference_arm_prints_the_same_config(capsys):
+    """The reference arm of bench.py (the reference's CPU algorithm for the layer) prints the same
+    metric, unit and config dict as the GPU arm, so the two lines compare like for like."""
+    import importlib.util
+    import json
+    import os
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    argv = sys.argv
+    sys.argv = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3",
+                "--ref-tokens", "16", "--gpus", "2"]
+    try:
+        bench.main()
+    finally:
+        sys.argv = argv
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["unit"] == bench.UNIT and line["config"] == bench.layer_config(2)
+    assert line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
+    assert line["scaling"] == "strong" and line["higher_is_better"] is True
