@@ -373,8 +373,8 @@ int gemm_common(const void* input, const void* weights, void* output, const int6
   p.k = static_cast<int>(k);
   p.sort_by_m = sort_by_m ? env_int("GGO_SEG_ORDER", 2) : 0;
   p.group_m = raster_group_m(k, 128);  // re-derived below for 256-row pair tiles
-  // Test hook for the bounded waits: GGO_TEST_INJECT_STALL=1 makes the first CTA leave one
-  // pipeline stage unarmed and lowers the wait limit to 2^24 cycles (~10 ms). The kernel then
+  // Test hook for the bounded waits: GGO_TEST_INJECT_STALL=1 makes the CTA that claims tile 0 leave
+  // its first pipeline stage unarmed and lowers the wait limit to 2^24 cycles (~10 ms). The kernel then
   // records a timeout in the workspace and returns; nothing faults or hangs.
   p.inject_stall = env_int("GGO_TEST_INJECT_STALL", 0) > 0 ? 1 : 0;
   p.wait_limit = p.inject_stall ? (1ll << 24) : GGO_WAIT_LIMIT_CYCLES;

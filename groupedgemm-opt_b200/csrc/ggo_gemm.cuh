@@ -89,7 +89,7 @@ struct GemmParams {
   void* peer_out[8];
   int use_tma_store;      // 1: the output tensor map is valid (plain output, 64-column boxes)
   long long wait_limit;   // bounded-wait limit in SM cycles
-  int inject_stall;       // test hook: CTA 0 never arms its first pipeline stage
+  int inject_stall;       // test hook: the tile claimed first never gets its first stage armed
   const float* row_scale; // kEpiScaled: one scale per input row
   const float* col_scale; // kEpiScaled: [num_experts, n_out] scales
   int split_mode;         // 0 all rows; 1 pair pass (no short tails); 2 short tails only
@@ -696,7 +696,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0, phase = 0, q = 0, qphase = 0;
       uint32_t armed = 0, armed_par = 0;  // stages whose loads were issued, and their parity
-      bool first_tile = true;
       while (true) {
         const int t = atomicAdd(&p.ws->tile_counter, 1);
         TileInfo info;
@@ -716,8 +715,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          // test hook: CTA 0 leaves its first stage unarmed, so the MMA's bounded wait expires
-          const bool skip = p.inject_stall && blockIdx.x == 0 && first_tile && kb == 0;
+          // test hook: the CTA that claimed tile 0 leaves that tile's first stage unarmed, so its
+          // MMA's bounded wait expires
+          const bool skip = p.inject_stall && t == 0 && kb == 0;
           if (!skip) {
             uint8_t* a_dst = tiles + stage * L::kStageBytes;
             uint8_t* b_dst = a_dst + L::kABytes;
@@ -743,7 +743,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
-        first_tile = false;
         if (!ok) break;
       }
       if (guard->abort) drain_armed_stages<S>(full_bar, armed, armed_par, guard->limit);

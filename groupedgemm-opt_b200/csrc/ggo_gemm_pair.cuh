@@ -167,11 +167,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0, phase = 0, q = 0, qphase = 0;
       uint32_t armed = 0, armed_par = 0;  // leader: stages armed, and their parity
-      bool first_tile = true;
       while (true) {
         TileInfo info;
+        bool stall_tile = false;  // test hook: this pair claimed tile 0
         if (leader) {
           const int t = atomicAdd(&p.ws->tile_counter, 1);
+          stall_tile = t == 0;
           info.rows = 0;
           if (t < total_tiles)
             info = decode_tile<kTileM, kOutBN, EPI, BN / 2, BMN>(
@@ -202,9 +203,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          // test hook: the first pair's leader leaves its first stage unarmed
-          const bool skip =
-              p.inject_stall && blockIdx.x == 0 && leader && first_tile && kb == 0;
+          // test hook: the leader of the pair that claimed tile 0 leaves its first stage unarmed
+          const bool skip = p.inject_stall && stall_tile && kb == 0;
           if (!skip) {
             uint8_t* a_dst = tiles + stage * L::kStageBytes;
             uint8_t* b_dst = a_dst + L::kABytes;
@@ -242,7 +242,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
-        first_tile = false;
         if (!ok) break;
       }
       // the leader's barriers count both CTAs' bytes; the final cluster barrier keeps the peer

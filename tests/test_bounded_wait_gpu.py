@@ -1,5 +1,6 @@
 """Failure detection on the GPU without a fault: a test hook (GGO_TEST_INJECT_STALL) makes the
-first CTA leave one pipeline stage unarmed and lowers the bounded-wait limit to ~10 ms. The kernel
+CTA that claims the first tile leave that tile's first pipeline stage unarmed and lowers the
+bounded-wait limit to ~10 ms. The kernel
 must return on its own, record a timeout in the workspace (read back as RuntimeError by
 check_device_errors) and leave the context usable: the next normal call is correct."""
 import time
