@@ -187,9 +187,10 @@ def _gather_floats(vals, world):
     return [o.tolist() for o in out]
 
 
-def _timed(fn, steps, world):
+def _timed(fn, steps, world, finish=None):
     """Device time of `steps` calls: events on the launching (current) stream, barrier + sync on
-    both sides, max over ranks. Returns (total_ms, per-step event times)."""
+    both sides, max over ranks. `finish` (optional) runs after the last call, before the closing
+    event, to order work of other streams before it. Returns (total_ms, per-step event times)."""
     import torch
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -201,6 +202,8 @@ def _timed(fn, steps, world):
         starts[i].record()
         fn()
         ends[i].record()
+    if finish is not None:
+        finish()
     t1.record()
     _barrier_sync(world)
     total = _max_over_ranks(t0.elapsed_time(t1), world)
@@ -227,13 +230,37 @@ def _min_over_ranks(x, world):
     return -_max_over_ranks(-x, world)
 
 
-def measure(fn, steps, world, local, warm_s=1.0):
-    """Warm loop >= warm_s under a clock sampler, then `steps` timed calls. Returns
-    (ms per call, per-call event times, clocks)."""
+def measure(fn, steps, world, local, warm_s=1.0, finish=None):
+    """Warm loop >= warm_s under a clock sampler, then `steps` timed calls (`finish` as in
+    _timed). Returns (ms per call, per-call event times, clocks)."""
     with ClockSampler(local) as clk:
         _warm(fn, world, warm_s)
-        total, per = _timed(fn, steps, world)
+        if finish is not None:
+            finish()
+        total, per = _timed(fn, steps, world, finish)
     return total / steps, per, clk.summary()
+
+
+def measure_burst(fn, steps, local, idle_s=1.0, reps=3):
+    """A kernel timed alone, as the burst peak (`bf16_tflops` of MEASURED_PEAKS.json) was: after
+    an idle gap that lets the GPU fall back under its power cap, `steps` back-to-back calls
+    (CUDA events on the launching stream); the median over `reps` gaps. Returns (ms per call,
+    clocks) -- the clock samples include the idle gaps."""
+    import torch
+    per = []
+    with ClockSampler(local) as clk:
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            time.sleep(idle_s)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(steps):
+                fn()
+            t1.record()
+            torch.cuda.synchronize()
+            per.append(t0.elapsed_time(t1) / steps)
+    return statistics.median(per), clk.summary()
 
 
 # ----------------------------------------------------------------------------- problems
@@ -325,7 +352,8 @@ def mixtral_layer_leg(world, rank, local, steps, warmup):
     parallelism on the fused peer-memory path, the NCCL all-to-all path timed beside it)."""
     import torch
     import torch.distributed as dist
-    from grouped_gemm_opt import EPBuffers, StageEvents, _C, fused_moe, fused_moe_host
+    from grouped_gemm_opt import (EPBuffers, MoEHostPipeline, StageEvents, _C, fused_moe,
+                                  fused_moe_host)
     T, H, F, Ex, k = MIX_T, MIX_H, MIX_F, MIX_E, MIX_K
     tl = T // world
     x_g, l_g, x, logits = _tokens(T, H, Ex, SEED_TOKENS, rank, world)
@@ -406,17 +434,30 @@ def mixtral_layer_leg(world, rank, local, steps, warmup):
     x_h = x.cpu().pin_memory()
     l_h = logits.cpu().pin_memory()
     o_h = torch.empty(tl, H, dtype=torch.bfloat16).pin_memory()
-    e2e_fn = lambda: fused_moe_host(x_h, l_h, wgu, wd, k, out=o_h, chunks=4,  # noqa: E731
-                                    ep_group=grp, ep_buffers=bufs)
-    ms_e, _, clk_e = measure(e2e_fn, steps, world, local)
-    torch.cuda.synchronize()
+    # (a) the streaming API: every step submits one batch (copy in, layer, copy out); batch
+    # i+1's copy in and batch i's copy out overlap the layers; the timed region ends once the
+    # last result is in host memory (the device-wide synchronize of _timed)
+    pipe = MoEHostPipeline(wgu, wd, k, ep_group=grp, ep_buffers=bufs)
+    ms_e, _, clk_e = measure(lambda: pipe.submit(x_h, l_h, o_h), steps, world, local,
+                             finish=lambda: torch.cuda.current_stream().wait_stream(pipe.s_out))
+    pipe.synchronize()
     outs["e2e_host"] = o_h.cuda()
+    # (b) one isolated call's latency path: fused_moe_host, token chunks overlapped on copy
+    # streams inside the call, joined back before the next call
+    single_fn = lambda: fused_moe_host(x_h, l_h, wgu, wd, k, out=o_h, chunks=4,  # noqa: E731
+                                       ep_group=grp, ep_buffers=bufs)
+    ms_s, _, clk_s = measure(single_fn, steps, world, local)
+    torch.cuda.synchronize()
+    outs["e2e_single_call"] = o_h.cuda()
     res["e2e"] = {"value": T / (ms_e / 1e3), "unit": UNIT,
                   "h2d_bytes_per_step": T * H * 2 + T * Ex * 4,
                   "d2h_bytes_per_step": T * H * 2,
-                  "api": "fused_moe_host (pinned host tokens/logits/result, 4 chunks "
-                         "overlapped on copy streams); bytes summed over all ranks",
-                  "ms": ms_e, "clocks": clk_e}
+                  "api": "MoEHostPipeline.submit per step (pinned host tokens/logits/result; "
+                         "copies of one step overlap the layer of the next); bytes summed over "
+                         "all ranks",
+                  "ms": ms_e, "clocks": clk_e,
+                  "single_call": {"value": T / (ms_s / 1e3), "ms": ms_s, "clocks": clk_s,
+                                  "api": "fused_moe_host, 4 token chunks, joined per call"}}
     if bufs is not None:
         bufs.check()
     res["ep_parity"] = ep_parity(outs, x_g, l_g, rank, world, H, F, k, SEED_EXPERTS, 32)
@@ -512,7 +553,22 @@ def grouped_gemm_leg(local, steps, warmup):
     y_h = torch.empty(T_TOK, N, dtype=torch.bfloat16).pin_memory()
     e2e_fn = lambda: ggo.grouped_gemm_opt_host(x_h, w, tpe_hp, out=y_h, chunks=8)  # noqa: E731
     ems, _, eclk = measure(e2e_fn, max(20, steps), 1, local)
+    # the kernel timed alone (bursts of 5 calls after idle gaps) against the burst peak, for
+    # uniform and skewed routing (north_star's two cfg2 cases), beside dense cuBLAS timed the same
+    # way; the sustained figures above are what a long run holds under the 1 kW cap
+    bursts = {}
+    for name, counts in (("uniform", tpe), ("skewed", _skewed_counts(T_TOK, E).cuda())):
+        f = lambda c=counts: ggo.grouped_gemm_opt(x, w, c)  # noqa: E731
+        bms, bclk = measure_burst(f, 5, local)
+        bursts[name] = {"ms": bms, "tflops": GEMM_FLOP / bms / 1e9,
+                        "frac_of_burst_peak": GEMM_FLOP / bms / 1e9 / burst, "clocks": bclk}
+    dbms, _ = measure_burst(dense, 5, local)
+    bursts["dense_cublas"] = {"ms": dbms, "tflops": GEMM_FLOP / dbms / 1e9}
+    bursts["vs_dense"] = dbms / bursts["uniform"]["ms"]
+    bursts["what"] = ("5 calls back to back after a 1 s idle gap, median of 3 gaps; against "
+                      "bf16_tflops (the burst peak)")
     return {"workload": "cfg2 grouped GEMM E8 T4096 K4096 N14336 bf16, uniform (configs[1])",
+            "burst": bursts,
             "value": GEMM_FLOP / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms": ms, "steps": st,
             "clocks": clk,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
@@ -769,7 +825,8 @@ def run_reference(args):
 def profile_run(args):
     """Minimal runs for ncu captures (warm-up + steps of one path, prints a done line):
     gemm (cfg2 grouped GEMM), fp8 / mxfp8 / dgrad / wgrad (cfg2 shapes), moe (the one-GPU
-    Mixtral layer), gemm1cta (cfg2 on the single-CTA 128x256 kernel), skinny (cfg3 zipf)."""
+    Mixtral layer), gemm1cta (cfg2 on the single-CTA 128x256 kernel), skinny (cfg3 zipf),
+    dsv3down (the DSv3 layer's down-projection shape, 64 experts)."""
     import torch
     torch.cuda.set_device(0)
     import grouped_gemm_opt as ggo
@@ -795,6 +852,15 @@ def profile_run(args):
             dy = torch.randn(T_TOK, N, device="cuda", generator=g).to(torch.bfloat16)
             fn = (lambda: _C.grouped_gemm_dgrad(dy, w, tpe, 4, True)) if args.profile == "dgrad" \
                 else (lambda: _C.grouped_gemm_wgrad(x, dy, tpe, True))
+    elif args.profile == "dsv3down":
+        # the DSv3 layer's down projection per expert (K=2048 -> N=7168, ~1024 rows per expert),
+        # 64 of its 256 experts (a few GB on the device)
+        ex, rows = 64, 65536
+        x = torch.randn(rows, 2048, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(ex, 7168, 2048, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        gc = torch.Generator().manual_seed(3)
+        tpe = torch.bincount(torch.randint(0, ex, (rows,), generator=gc), minlength=ex).cuda()
+        fn = lambda: ggo.grouped_gemm_opt(x, w, tpe)  # noqa: E731
     elif args.profile == "skinny":
         x = torch.randn(8192, 4096, device="cuda", generator=g).to(torch.bfloat16)
         w = (torch.randn(64, 14336, 4096, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
@@ -823,7 +889,7 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=0,
                     help="reference arm: tokens per step (default: the whole layer)")
     ap.add_argument("--profile", choices=["gemm", "gemm1cta", "moe", "fp8", "mxfp8", "dgrad",
-                                          "wgrad", "skinny"], default=None,
+                                          "wgrad", "skinny", "dsv3down"], default=None,
                     help="minimal run for ncu captures: warm-up + steps of one path, no JSON")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

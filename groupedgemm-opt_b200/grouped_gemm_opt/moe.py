@@ -384,6 +384,65 @@ def fused_moe_host(
     return out
 
 
+class MoEHostPipeline:
+    """Streams batches of HOST-resident tokens through :func:`fused_moe`, batch after batch, the
+    way a server feeds a layer: each :meth:`submit` copies its batch's tokens and logits in on a
+    copy stream, runs the layer on the current stream once they have landed, and copies the
+    result out to host memory on a second copy stream. Nothing joins the copy streams back to
+    the current stream, so batch i+1's copy in and batch i's copy out run while the layer
+    computes: in steady state the PCIe traffic of a batch costs no layer time. Each batch is one
+    whole layer call (no token chunking, which would cost GEMM efficiency).
+
+    Results are complete after :meth:`synchronize` (or a device-wide synchronize). Host buffers
+    passed to :meth:`submit` must stay untouched until then. Every rank of an expert-parallel
+    group submits the same number of batches in the same order (each is a collective)."""
+
+    def __init__(self, w_gate_up: torch.Tensor, w_down: torch.Tensor, top_k: int,
+                 ep_group: Optional[dist.ProcessGroup] = None,
+                 ep_buffers: Optional[EPBuffers] = None, sort_by_m: bool = True):
+        assert w_gate_up.is_cuda and w_down.is_cuda
+        self.w_gate_up, self.w_down, self.top_k = w_gate_up, w_down, top_k
+        self.ep_group, self.ep_buffers, self.sort_by_m = ep_group, ep_buffers, sort_by_m
+        self.device = w_gate_up.device
+        self.s_in = torch.cuda.Stream(self.device)
+        self.s_out = torch.cuda.Stream(self.device)
+
+    def submit(self, hidden: torch.Tensor, router_logits: torch.Tensor,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Enqueue one batch: ``hidden`` [T, H] and ``router_logits`` [T, E] in (pinned) host
+        memory; the result goes to ``out`` [T, H] in host memory (allocated pinned if None),
+        which is returned at once and is valid after :meth:`synchronize`."""
+        assert not hidden.is_cuda and not router_logits.is_cuda, "tokens must be in host memory"
+        if out is None:
+            out = torch.empty(hidden.shape, dtype=hidden.dtype, pin_memory=True)
+        main = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.s_in):
+            x = hidden.to(self.device, non_blocking=True)
+            lg = router_logits.to(self.device, non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(self.s_in)
+        main.wait_event(landed)
+        y = fused_moe(x, lg, self.w_gate_up, self.w_down, self.top_k, ep_group=self.ep_group,
+                      sort_by_m=self.sort_by_m, ep_buffers=self.ep_buffers)
+        x.record_stream(main)
+        lg.record_stream(main)
+        done = torch.cuda.Event()
+        done.record(main)
+        self.s_out.wait_event(done)
+        with torch.cuda.stream(self.s_out):
+            out.copy_(y, non_blocking=True)
+            y.record_stream(self.s_out)
+        return out
+
+    def synchronize(self) -> None:
+        """Wait until every submitted batch's result is in host memory; afterwards the current
+        stream is ordered after all of the pipeline's work."""
+        main = torch.cuda.current_stream(self.device)
+        main.wait_stream(self.s_in)
+        main.wait_stream(self.s_out)
+        self.s_out.synchronize()
+
+
 @dataclass
 class MoEFP8Weights:
     """e4m3 expert weights with one fp32 scale per output channel (see quantize_moe_weights)."""

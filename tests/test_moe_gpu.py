@@ -217,3 +217,25 @@ def test_dsv3_decode_layer_token_sample():
     ref = oracle.moe_tokens(x[sel.to(DEV)].cpu(), logits[sel.to(DEV)].cpu(),
                             lambda e: (wgu[e].cpu(), wd[e].cpu()), k, round_to=torch.bfloat16)
     assert_parity(out[sel.to(DEV)], ref, "dsv3 decode sample")
+
+
+def test_host_pipeline_streams_batches():
+    """MoEHostPipeline: three batches of different sizes submitted back to back (copies of one
+    batch overlapping the layer of another) give each batch's device-layer result."""
+    from grouped_gemm_opt import MoEHostPipeline, fused_moe
+    g = torch.Generator().manual_seed(13)
+    H, F, E, k = 512, 768, 8, 2
+    wgu, wd = _moe_weights(E, H, F, seed=5)
+    wgu, wd = wgu.to(DEV), wd.to(DEV)
+    pipe = MoEHostPipeline(wgu, wd, k)
+    batches, outs = [], []
+    for T in (700, 1, 1300):
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory()
+        logits = torch.randn(T, E, generator=g).pin_memory()
+        batches.append((x, logits))
+        outs.append(pipe.submit(x, logits))
+    pipe.synchronize()
+    for (x, logits), out in zip(batches, outs):
+        assert not out.is_cuda and out.shape == x.shape
+        ref = fused_moe(x.to(DEV), logits.to(DEV), wgu, wd, k).cpu()
+        assert torch.equal(out, ref), f"pipeline batch of {x.size(0)} tokens differs"
