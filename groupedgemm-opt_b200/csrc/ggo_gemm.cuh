@@ -479,10 +479,10 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
 #pragma unroll 1
     for (int b = 0; b < kBoxes; ++b) {
       const int c64 = 64 * ((first_box + b) % kBoxes);
-      if (b > 0) {  // the previous box's store has read the staging buffer
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-      }
+      // the previous box's store -- for box 0 the last store of this warp's previous tile -- has
+      // finished reading the staging buffer
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const uint32_t chunk = static_cast<uint32_t>(q ^ (lane & 7));
@@ -510,7 +510,7 @@ __device__ __forceinline__ void store_tile_rows(uint32_t t_row, int n0, int n_ou
 #pragma unroll 1
   for (int b = 0; b < kBoxes; ++b) {
     const int c64 = 64 * ((first_box + b) % kBoxes);
-    if (warp_tma && b > 0) {  // the previous box's store has read the staging buffer
+    if (warp_tma) {  // the previous box's store (for box 0: of the previous tile) has read it
       if (lane == 0) bulk_wait_read_all();
       __syncwarp();
     }
